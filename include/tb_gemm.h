@@ -1,0 +1,159 @@
+/*
+ * tb_gemm.h — C ABI of the B200-native `tb.matmul` GEMM.
+ *
+ * The reference (zrqnwu/mini_triton_nvgpu_v1) has no runtime library: its
+ * operator surface is the MLIR op
+ *
+ *     tb.matmul %A, %B, %C {block_m, block_n, block_k, group_m, exact_tile}
+ *
+ * (include/tb/IR/TBOps.td:32-58) plus the module attributes tb.num-warps,
+ * tb.requested-stages (include/tb/Analysis/TargetInfo.h:17-21), tb.split-k,
+ * tb.reduction-mode, tb.persistent, tb.programs-per-tile
+ * (include/tb/Analysis/ProgramMappingPlan.h:14-17) and tb.num-ctas
+ * (TargetInfo.h:20). `tb-opt` lowers that op into one kernel
+ * `kernel_tb_kernel_0(A, B, C)` that computes C = C_in + A·B in place
+ * (lib/Transforms/LowerPipelineToNVGPU.cpp:994-999, :2507-2583).
+ *
+ * This header replaces that whole chain with three steps:
+ *   tb_matmul_desc  — the knobs, same names and meaning as the attributes;
+ *   tb_matmul_plan  — validated knobs + program mapping (replaces
+ *                     verifySupportedKernelConfig, deriveProgramMappingPlan,
+ *                     deriveReductionPlan, derivePersistentWorkPlan);
+ *   tb_matmul_run   — one stream-ordered launch of the sm_100a kernels
+ *                     (replaces the generated kernel and its launch).
+ *
+ * Ownership: the caller owns every device buffer and the stream. A plan owns
+ * host metadata only; it is immutable after creation and may be shared by
+ * threads. Every call returns a tbStatus; tb_last_error() gives the message of
+ * the calling thread's last failure (messages mirror the reference's
+ * diagnostics where the rule is the reference's).
+ */
+#ifndef TB_GEMM_H_
+#define TB_GEMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tbStatus {
+  TB_OK = 0,
+  TB_ERR_INVALID_ARGUMENT = 1, /* knob or argument rejected by validation */
+  TB_ERR_UNSUPPORTED = 2,      /* legal for the reference, outside this build */
+  TB_ERR_CUDA = 3,             /* a CUDA runtime/driver call failed */
+  TB_ERR_DEVICE_TIMEOUT = 4,   /* a bounded device-side wait gave up */
+  TB_ERR_WORKSPACE = 5,        /* workspace missing or too small */
+  TB_ERR_NCCL = 6              /* NCCL unavailable or a collective failed */
+} tbStatus;
+
+/* Element types (memref element types of A, B and C). */
+typedef enum tbDtype { TB_F16 = 0, TB_F32 = 1, TB_BF16 = 2 } tbDtype;
+
+/* tb.reduction-mode (ProgramMappingPlan.h:37-41). UNSET means the attribute
+ * is absent, which the reference resolves to split_k_serial
+ * (lib/Analysis/ProgramMappingPlan.cpp:415-418). */
+typedef enum tbReductionMode {
+  TB_REDUCTION_UNSET = 0,
+  TB_REDUCTION_SPLIT_K_SERIAL = 1,   /* fp32 workspace + fixed-order reduction */
+  TB_REDUCTION_SPLIT_K_PARALLEL = 2  /* f32 atomic accumulation into C */
+} tbReductionMode;
+
+/* Knobs of one tb.matmul. Field names follow the reference attributes. */
+typedef struct tb_matmul_desc {
+  int64_t m, n, k;                 /* A: m×k, B: k×n, C: m×n (static shapes) */
+  int64_t block_m, block_n, block_k; /* TBOps.td:42-44 */
+  int64_t group_m;                 /* TBOps.td:45, default 8 */
+  int32_t exact_tile;              /* TBOps.td:46, default 1 */
+  int64_t num_warps;               /* "tb.num-warps" (required) */
+  int64_t num_stages;              /* "tb.requested-stages" (required) */
+  int64_t split_k;                 /* "tb.split-k", default 1 */
+  int32_t reduction_mode;          /* "tb.reduction-mode", tbReductionMode */
+  int32_t persistent;              /* "tb.persistent", default 0 */
+  int64_t num_ctas;                /* "tb.num-ctas", default 1 */
+  int64_t programs_per_tile;       /* "tb.programs-per-tile", 0 = absent */
+  int32_t a_dtype, b_dtype;        /* must be TB_F16 */
+  int32_t c_dtype;                 /* TB_F32 (reference) or TB_F16 (extension) */
+  int32_t beta;                    /* 1: C = C_in + A·B (reference); 0: C = A·B */
+} tb_matmul_desc;
+
+typedef struct tb_matmul_plan tb_matmul_plan;
+
+/* Work assigned to one program id (LowerPipelineToNVGPU.cpp:279-357). */
+typedef struct tb_program_work {
+  int64_t tile_m, tile_n, split_part;
+  int64_t k_tile_begin, k_tile_count; /* in block_k tiles */
+} tb_program_work;
+
+/* Fills the defaults the reference applies to absent attributes:
+ * group_m=8, exact_tile=1, split_k=1, num_ctas=1, persistent=0,
+ * f16·f16→f32, beta=1. Replaces the attribute defaults of TBOps.td:45-46 and
+ * ProgramMappingPlan.cpp:331-340. */
+tbStatus tb_matmul_desc_init(tb_matmul_desc* desc);
+
+/* Validates `desc` and derives the program mapping. `device` < 0 plans for a
+ * B200 (148 SMs) without touching CUDA, for host-only use; otherwise the SM
+ * count of `device` is queried. Replaces verifySupportedKernelConfig
+ * (lib/Analysis/KernelConfig.cpp:202-246), deriveProgramMappingPlan
+ * (lib/Analysis/ProgramMappingPlan.cpp:329-458), deriveReductionPlan
+ * (lib/Analysis/ReductionPlan.cpp:137-192), derivePersistentWorkPlan
+ * (lib/Analysis/PersistentWorkPlan.cpp:91-131) and the mapping checks of
+ * validateLoweringContract (LowerPipelineToNVGPU.cpp:678-815). */
+tbStatus tb_matmul_plan_create(const tb_matmul_desc* desc, int device,
+                               tb_matmul_plan** plan);
+
+tbStatus tb_matmul_plan_destroy(tb_matmul_plan* plan);
+
+/* Bytes of device workspace `tb_matmul_run` needs (nonzero only for
+ * split_k_serial, which keeps S fp32 partials of C). Replaces the global
+ * scratch of ReductionPlan (scratchBytes, ReductionPlan.cpp:164-166). */
+size_t tb_matmul_workspace_bytes(const tb_matmul_plan* plan);
+
+/* Writes a JSON object describing the plan (the reference's structural plan
+ * facts — mapping_kind, swizzle_kind, total_programs, reduction kind,
+ * resident_programs, warp_grid, … — and this build's launch facts) into buf.
+ * Replaces the plan attributes tb-opt prints (checked by the reference's
+ * test/Transforms FileCheck tests). Returns TB_ERR_INVALID_ARGUMENT
+ * when len is too small; *needed receives the size including the NUL. */
+tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* buf,
+                                 size_t len, size_t* needed);
+
+/* The work of program `pid` (0 <= pid < total_programs). Host restatement of
+ * buildProgramWorkAssignment + buildSplitKGroupActivePredicate
+ * (LowerPipelineToNVGPU.cpp:279-357); the device kernels use the same code. */
+tbStatus tb_matmul_program_work(const tb_matmul_plan* plan, int64_t pid,
+                                tb_program_work* work);
+
+/* Runs C = beta·C_in + A·B in place on `stream` (a cudaStream_t; NULL = the
+ * legacy default stream). A is m×k row-major with row stride lda (elements),
+ * B is k×n row-major with stride ldb, C is m×n row-major with stride ldc, of
+ * c_dtype. lda and ldb must be multiples of 8 and A/B 16-byte aligned (TMA).
+ * `workspace` must hold tb_matmul_workspace_bytes(plan) bytes (may be NULL
+ * when that is 0). Replaces kernel_tb_kernel_0(A, B, C) and its launch
+ * (LowerPipelineToNVGPU.cpp:2678-2711; tools/bench_stage1_fair.py:67-74). */
+tbStatus tb_matmul_run(const tb_matmul_plan* plan, const void* A, int64_t lda,
+                       const void* B, int64_t ldb, void* C, int64_t ldc,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* One-call convenience: desc → plan → run → destroy. */
+tbStatus tb_matmul(const tb_matmul_desc* desc, const void* A, int64_t lda,
+                   const void* B, int64_t ldb, void* C, int64_t ldc,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reads and clears the device status word the kernels set when a bounded
+ * wait gives up (TB_ERR_DEVICE_TIMEOUT) — synchronises `stream`. The reference
+ * has no device-side failure detection; this has no counterpart there. */
+tbStatus tb_device_status(void* stream, uint32_t* raw_status);
+
+/* Message of the calling thread's most recent failure ("" if none). */
+const char* tb_last_error(void);
+
+/* Library version string. */
+const char* tb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TB_GEMM_H_ */

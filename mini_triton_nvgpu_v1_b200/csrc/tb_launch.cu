@@ -1,0 +1,647 @@
+// tb_launch.cu — the sm_100a `tb.matmul` kernels and their launcher.
+//
+// One kernel family replaces the reference's generated
+// `kernel_tb_kernel_0` (cp.async → ldmatrix → mma.sync, statically unrolled
+// over K/16; LowerPipelineToNVGPU.cpp:2019-2607) with a warp-specialised,
+// persistent tcgen05 pipeline:
+//
+//   warp 0 (one lane)  TMA producer: A box [128 × 64] (K-major) and B boxes
+//                      [64 × 64] (N-major), both 128-byte swizzled, into an
+//                      S-deep shared-memory ring guarded by full/empty
+//                      mbarriers.
+//   warp 1 (one lane)  MMA issuer: tcgen05.mma kind::f16, M=128, N=BN, K=16
+//                      per instruction into one of two TMEM accumulators;
+//                      tcgen05.commit frees ring stages and publishes tiles.
+//   warps 2-5          epilogue: tcgen05.ld TMEM → registers, adds C_in
+//                      (the reference's C-init, :2192-2278), masked stores
+//                      (the boundary-aware epilogue, EpiloguePlan.cpp:864-979),
+//                      or split-K partial / atomic output (:1862-1912).
+//
+// Each CTA walks program ids pid = blockIdx.x, blockIdx.x + gridDim.x, …
+// and maps each with tb::program_work — the reference's mapping formulas —
+// so tile, grouped, split-K and persistent mappings compute exactly the
+// reference's (tile, split part) set. Double-buffered TMEM lets the
+// epilogue of one program overlap the mainloop of the next.
+//
+// Every wait is bounded: when a wait runs past kWaitBudgetCycles the thread
+// records TB_ERR_DEVICE_TIMEOUT in g_tb_status, raises a CTA-wide abort flag
+// and every role leaves its loop; in-flight TMA loads and MMAs are drained
+// (with bounded waits) before TMEM is released.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "tb_plan.h"
+#include "tb_sm100.cuh"
+
+using namespace tb::sm100;
+
+__device__ uint32_t g_tb_status = 0;
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kBK = 64;               // K elements per ring stage (128-byte rows)
+constexpr int kCtaM = 128;            // tcgen05 M
+constexpr uint32_t kABytes = kCtaM * kBK * 2;
+constexpr uint32_t kBBoxBytes = 64 * kBK * 2;  // one [64 k × 64 n] box
+constexpr size_t kSmemLimit = 232448;  // 227 KB opt-in per CTA
+constexpr long long kWaitBudgetCycles = 2000000000LL;  // ≈1 s at 1.9 GHz
+
+constexpr uint32_t kSiteProducer = 1, kSiteMma = 2, kSiteEpilogue = 3, kSiteDrain = 4;
+
+template <int BN>
+struct Cfg {
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr int kRawStages = (int)((kSmemLimit - 1024 - 512) / kStageBytes);
+  static constexpr int kStages = kRawStages > 8 ? 8 : kRawStages;
+  static constexpr uint32_t kTmemCols = 2 * BN;  // 128, 256 or 512: powers of two
+  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 512;
+};
+
+struct KParams {
+  tb::MappingArgs map;
+  int32_t M, N, K;
+  int32_t block_m, block_n, block_k;
+  int32_t epilogue;  // TbEpilogue
+  int32_t beta;
+  int32_t vec_c;     // C rows allow 16-byte vector access
+  int32_t vec_ws;    // workspace rows allow 16-byte vector access
+  void* C;
+  int64_t ldc;
+  float* ws;
+};
+
+__device__ __forceinline__ void record_error(uint32_t code, uint32_t site) {
+  const uint32_t v = (code << 24) | (site << 16) | (blockIdx.x & 0xFFFFu);
+  atomicCAS(&g_tb_status, 0u, v);
+}
+
+// Bounded wait: false when the abort flag is up or the budget ran out.
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity,
+                                             volatile int* abort_flag, uint32_t site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      record_error(TB_ERR_DEVICE_TIMEOUT, site);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+struct Extent {
+  int32_t m0, n0, rows, cols, k_begin, k_end, nkb, part;
+};
+
+__device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pid) {
+  const tb::Work w = tb::program_work(p.map, pid);
+  Extent e;
+  e.m0 = w.tile_m * p.block_m;
+  e.n0 = w.tile_n * p.block_n;
+  e.rows = min(p.block_m, p.M - e.m0);
+  e.cols = min(p.block_n, p.N - e.n0);
+  e.k_begin = w.kt_begin * p.block_k;
+  e.k_end = min(p.K, (w.kt_begin + w.kt_count) * p.block_k);
+  e.nkb = e.k_end > e.k_begin ? (e.k_end - e.k_begin + kBK - 1) / kBK : 0;
+  e.part = w.part;
+  return e;
+}
+
+template <typename OutT>
+struct OutIO;
+
+template <>
+struct OutIO<float> {
+  static __device__ __forceinline__ float load(const float* p) { return *p; }
+  static __device__ __forceinline__ void store(float* p, float v) { *p = v; }
+  // 32 consecutive values, 16-byte aligned.
+  static __device__ __forceinline__ void load32(const float* p, float (&c)[32]) {
+    const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 t = q[i];
+      c[4 * i] = t.x; c[4 * i + 1] = t.y; c[4 * i + 2] = t.z; c[4 * i + 3] = t.w;
+    }
+  }
+  static __device__ __forceinline__ void store32(float* p, const float (&v)[32]) {
+    float4* q = reinterpret_cast<float4*>(p);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+};
+
+template <>
+struct OutIO<__half> {
+  static __device__ __forceinline__ float load(const __half* p) { return __half2float(*p); }
+  static __device__ __forceinline__ void store(__half* p, float v) { *p = __float2half_rn(v); }
+  static __device__ __forceinline__ void load32(const __half* p, float (&c)[32]) {
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 t = q[i];
+      const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __half2 h = *reinterpret_cast<const __half2*>(&w[j]);
+        const float2 f = __half22float2(h);
+        c[8 * i + 2 * j] = f.x;
+        c[8 * i + 2 * j + 1] = f.y;
+      }
+    }
+  }
+  static __device__ __forceinline__ void store32(__half* p, const float (&v)[32]) {
+    uint4* q = reinterpret_cast<uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __half2 h = __floats2half2_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+        w[j] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      q[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+};
+
+template <int BN, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    tb_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
+                         const __grid_constant__ CUtensorMap tmB, const KParams p) {
+  using C = Cfg<BN>;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + (size_t)S * kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)S * C::kBBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = bars + 2 * S + 2;
+  uint64_t* drain = bars + 2 * S + 4;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_addr(&tfull[a]), 1);
+      mbar_init(smem_addr(&tempty[a]), 4);
+    }
+    mbar_init(smem_addr(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_holder), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      for (int32_t pid = blockIdx.x; pid < p.map.total_programs; pid += gridDim.x) {
+        const Extent e = program_extent(p, pid);
+        bool ok = true;
+        for (int kb = 0; kb < e.nkb; ++kb) {
+          if (!wait_bounded(smem_addr(&empty[stage]), phase ^ 1u, abort_flag, kSiteProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_addr(&full[stage]);
+          mbar_expect_tx(fb, C::kStageBytes);
+          const int32_t kx = e.k_begin + kb * kBK;
+          tma_load_2d(smem_addr(sA + (size_t)stage * kABytes), &tmA, fb, kx, e.m0);
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(smem_addr(sB + (size_t)stage * C::kBBytes + (size_t)j * kBBoxBytes), &tmB, fb,
+                        e.n0 + 64 * j, kx);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+      // Drain: the newest fill of each stage must land before the CTA exits.
+      const long long last = issued < S ? issued : S;
+      for (long long i = 0; i < last; ++i) {
+        const long long f = issued - 1 - i;
+        const int s = (int)(f % S);
+        const uint32_t par = (uint32_t)((f / S) & 1);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(smem_addr(&full[s]), par)) {
+          if (clock64() - t0 > kWaitBudgetCycles) {
+            record_error(TB_ERR_DEVICE_TIMEOUT, kSiteDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(kCtaM, BN, 0, 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool issued_any = false;
+      bool ok = true;
+      for (int32_t pid = blockIdx.x; pid < p.map.total_programs && ok; pid += gridDim.x) {
+        const Extent e = program_extent(p, pid);
+        if (!wait_bounded(smem_addr(&tempty[acc]), acc_phase ^ 1u, abort_flag, kSiteMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        if (e.nkb == 0) {
+          mbar_arrive(smem_addr(&tfull[acc]));
+        } else {
+          for (int kb = 0; kb < e.nkb; ++kb) {
+            if (!wait_bounded(smem_addr(&full[stage]), phase, abort_flag, kSiteMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const int kvalid = min(kBK, e.k_end - (e.k_begin + kb * kBK));
+            const int nk16 = (kvalid + 15) / 16;
+            const uint32_t a0 = smem_addr(sA + (size_t)stage * kABytes);
+            const uint32_t b0 = smem_addr(sB + (size_t)stage * C::kBBytes);
+            for (int kk = 0; kk < nk16; ++kk) {
+              // A: K-major rows of 128 B; 8-row groups 1024 B apart; a K step
+              // of 16 elements is 32 B inside the swizzle atom.
+              const uint64_t da = smem_desc_sw128(a0 + kk * 32, 16, 1024);
+              // B: N-major; 64-column boxes kBBoxBytes apart (LBO), 8-row K
+              // groups 1024 B apart (SBO); 16 K rows are 2048 B.
+              const uint64_t db = smem_desc_sw128(b0 + kk * 2048, kBBoxBytes, 1024);
+              umma_f16(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+            issued_any = true;
+            umma_commit(smem_addr(&empty[stage]));
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (!ok) break;
+          umma_commit(smem_addr(&tfull[acc]));
+        }
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (!ok && issued_any) {
+        // Aborted with MMAs possibly in flight: wait for them before TMEM goes.
+        umma_commit(smem_addr(drain));
+        const long long t0 = clock64();
+        while (!mbar_try_wait(smem_addr(drain), 0)) {
+          if (clock64() - t0 > kWaitBudgetCycles) {
+            record_error(TB_ERR_DEVICE_TIMEOUT, kSiteDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int32_t pid = blockIdx.x; pid < p.map.total_programs; pid += gridDim.x) {
+      const Extent e = program_extent(p, pid);
+      int ok = 0;
+      if (lane == 0) ok = wait_bounded(smem_addr(&tfull[acc]), acc_phase, abort_flag, kSiteEpilogue);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const bool row_ok = row_in_tile < e.rows;
+      const int64_t grow = (int64_t)e.m0 + row_in_tile;
+      for (int c0 = 0; c0 < e.cols; c0 += 32) {
+        float v[32];
+        if (e.nkb > 0) {
+          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c0), v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+        if (!row_ok) continue;
+        const int ncol = min(32, e.cols - c0);
+        const int64_t gcol = (int64_t)e.n0 + c0;
+        if (p.epilogue == kEpiStore) {
+          OutT* dst = reinterpret_cast<OutT*>(p.C) + grow * p.ldc + gcol;
+          if (ncol == 32 && p.vec_c) {
+            if (p.beta) {
+              float c[32];
+              OutIO<OutT>::load32(dst, c);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += c[i];
+            }
+            OutIO<OutT>::store32(dst, v);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (i < ncol) {
+                float r = v[i];
+                if (p.beta) r += OutIO<OutT>::load(dst + i);
+                OutIO<OutT>::store(dst + i, r);
+              }
+            }
+          }
+        } else if (p.epilogue == kEpiWorkspace) {
+          float* dst = p.ws + ((int64_t)e.part * p.M + grow) * p.N + gcol;
+          if (ncol == 32 && p.vec_ws) {
+            OutIO<float>::store32(dst, v);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < ncol) dst[i] = v[i];
+          }
+        } else {  // kEpiAtomic: f32 C only
+          float* dst = reinterpret_cast<float*>(p.C) + grow * p.ldc + gcol;
+          if (ncol == 32 && p.vec_c) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              atomicAdd(reinterpret_cast<float4*>(dst) + i,
+                        make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < ncol) atomicAdd(dst + i, v[i]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&tempty[acc]));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// C = beta·C_in + Σ_s ws[s] in a fixed order (split_k_serial): deterministic.
+template <typename OutT>
+__global__ void __launch_bounds__(256)
+    tb_splitk_reduce_kernel(const float* __restrict__ ws, int32_t S, int32_t M, int32_t N,
+                            void* Cv, int64_t ldc, int32_t beta, int32_t vec) {
+  OutT* C = reinterpret_cast<OutT*>(Cv);
+  const int64_t plane = (int64_t)M * N;
+  if (vec) {  // N % 4 == 0 and C rows 16-byte aligned (f32) / 8-byte (f16)
+    const int64_t nvec = plane / 4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t e = i * 4;
+      const int64_t r = e / N, c = e % N;
+      float4 acc = reinterpret_cast<const float4*>(ws)[i];
+      for (int s = 1; s < S; ++s) {
+        const float4 t = reinterpret_cast<const float4*>(ws + s * plane)[i];
+        acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
+      }
+      OutT* dst = C + r * ldc + c;
+      if (beta) {
+        acc.x += OutIO<OutT>::load(dst);
+        acc.y += OutIO<OutT>::load(dst + 1);
+        acc.z += OutIO<OutT>::load(dst + 2);
+        acc.w += OutIO<OutT>::load(dst + 3);
+      }
+      OutIO<OutT>::store(dst, acc.x);
+      OutIO<OutT>::store(dst + 1, acc.y);
+      OutIO<OutT>::store(dst + 2, acc.z);
+      OutIO<OutT>::store(dst + 3, acc.w);
+    }
+  } else {
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < plane;
+         e += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t r = e / N, c = e % N;
+      float acc = ws[e];
+      for (int s = 1; s < S; ++s) acc += ws[s * plane + e];
+      OutT* dst = C + r * ldc + c;
+      if (beta) acc += OutIO<OutT>::load(dst);
+      OutIO<OutT>::store(dst, acc);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+cudaError_t g_encode_err = cudaSuccess;
+
+tbStatus get_encoder() {
+  std::call_once(g_encode_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    g_encode_err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (g_encode_err == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode)
+    return tb_fail(TB_ERR_CUDA, std::string("cuTensorMapEncodeTiled unavailable: ") +
+                                    cudaGetErrorString(g_encode_err));
+  return TB_OK;
+}
+
+// Row-major f16 matrix rows × cols with row stride ld (elements), boxed
+// [box_rows × 64] with 128-byte swizzle; out-of-range elements read as 0.
+tbStatus encode_f16_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                       uint32_t box_rows, const char* what) {
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return tb_fail(TB_ERR_CUDA, std::string("cuTensorMapEncodeTiled(") + what +
+                                    ") failed with CUresult " + std::to_string((int)r));
+  return TB_OK;
+}
+
+constexpr int kMaxDevices = 64;
+std::atomic<bool> g_attr_set[3][2][kMaxDevices];
+
+template <int BN, typename OutT>
+tbStatus launch_gemm(const tb_matmul_plan* plan, const CUtensorMap& ta, const CUtensorMap& tb_,
+                     const KParams& kp, cudaStream_t stream, int kt, int ot) {
+  auto kern = tb_gemm_sm100_kernel<BN, OutT>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices || !g_attr_set[kt][ot][dev].load()) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg<BN>::kSmem);
+    if (e != cudaSuccess)
+      return tb_fail(TB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    if (dev >= 0 && dev < kMaxDevices) g_attr_set[kt][ot][dev].store(true);
+  }
+  kern<<<(unsigned)plan->grid, kThreads, Cfg<BN>::kSmem, stream>>>(ta, tb_, kp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return tb_fail(TB_ERR_CUDA, std::string("tb_gemm_sm100 launch: ") + cudaGetErrorString(e));
+  return TB_OK;
+}
+
+template <typename OutT>
+tbStatus dispatch_tile(const tb_matmul_plan* plan, const CUtensorMap& ta, const CUtensorMap& tb_,
+                       const KParams& kp, cudaStream_t stream, int ot) {
+  switch (plan->kernel_tile) {
+    case kTile128x64: return launch_gemm<64, OutT>(plan, ta, tb_, kp, stream, 0, ot);
+    case kTile128x128: return launch_gemm<128, OutT>(plan, ta, tb_, kp, stream, 1, ot);
+    case kTile128x256: return launch_gemm<256, OutT>(plan, ta, tb_, kp, stream, 2, ot);
+  }
+  return tb_fail(TB_ERR_UNSUPPORTED, "unknown kernel tile");
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+size_t tb_kernel_smem_bytes(int32_t kernel_tile, int32_t /*stages*/) {
+  switch (kernel_tile) {
+    case kTile128x64: return Cfg<64>::kSmem;
+    case kTile128x128: return Cfg<128>::kSmem;
+    case kTile128x256: return Cfg<256>::kSmem;
+  }
+  return 0;
+}
+
+int32_t tb_kernel_max_stages(int32_t kernel_tile) {
+  switch (kernel_tile) {
+    case kTile128x64: return Cfg<64>::kStages;
+    case kTile128x128: return Cfg<128>::kStages;
+    case kTile128x256: return Cfg<256>::kStages;
+  }
+  return 0;
+}
+
+tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda, const void* B,
+                   int64_t ldb, void* Cp, int64_t ldc, void* workspace, size_t workspace_bytes,
+                   void* stream_v) {
+  const tb_matmul_desc& d = plan->desc;
+  if (!A || !B || !Cp) return tb_fail(TB_ERR_INVALID_ARGUMENT, "A, B and C must not be NULL");
+  if (lda < d.k || ldb < d.n || ldc < d.n)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "leading dimensions must be >= the row length");
+  if (lda % 8 != 0 || ldb % 8 != 0)
+    return tb_fail(TB_ERR_UNSUPPORTED,
+                   "lda and ldb must be multiples of 8 elements (16-byte TMA strides)");
+  if (!aligned16(A) || !aligned16(B))
+    return tb_fail(TB_ERR_UNSUPPORTED, "A and B must be 16-byte aligned (TMA)");
+  if (plan->workspace_bytes > 0 && (!workspace || workspace_bytes < plan->workspace_bytes))
+    return tb_fail(TB_ERR_WORKSPACE, "split_k_serial needs a workspace of " +
+                                         std::to_string(plan->workspace_bytes) + " bytes");
+  if (d.m > INT32_MAX || d.n > INT32_MAX || d.k > INT32_MAX)
+    return tb_fail(TB_ERR_UNSUPPORTED, "problem dimensions must fit in 32 bits");
+  tbStatus st = get_encoder();
+  if (st != TB_OK) return st;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_v);
+
+  CUtensorMap ta, tbm;
+  st = encode_f16_2d(&ta, A, d.m, d.k, lda, kCtaM, "A");
+  if (st != TB_OK) return st;
+  st = encode_f16_2d(&tbm, B, d.k, d.n, ldb, kBK, "B");
+  if (st != TB_OK) return st;
+
+  const size_t out_bytes = d.c_dtype == TB_F16 ? 2 : 4;
+  KParams kp;
+  kp.map = plan->map;
+  kp.M = (int32_t)d.m;
+  kp.N = (int32_t)d.n;
+  kp.K = (int32_t)d.k;
+  kp.block_m = (int32_t)d.block_m;
+  kp.block_n = (int32_t)d.block_n;
+  kp.block_k = (int32_t)d.block_k;
+  kp.epilogue = plan->epilogue;
+  kp.beta = d.beta ? 1 : 0;
+  kp.vec_c = aligned16(Cp) && ((ldc * (int64_t)out_bytes) % 16 == 0) &&
+             ((d.block_n * (int64_t)out_bytes) % 16 == 0);
+  kp.vec_ws = (d.n % 4 == 0) && (d.block_n % 4 == 0) && aligned16(workspace);
+  kp.C = Cp;
+  kp.ldc = ldc;
+  kp.ws = reinterpret_cast<float*>(workspace);
+
+  if (plan->epilogue == kEpiAtomic && !d.beta) {
+    // C = A·B through atomics: start from zero.
+    cudaError_t e = cudaMemset2DAsync(Cp, (size_t)ldc * 4, 0, (size_t)d.n * 4, (size_t)d.m, stream);
+    if (e != cudaSuccess)
+      return tb_fail(TB_ERR_CUDA, std::string("cudaMemset2DAsync: ") + cudaGetErrorString(e));
+  }
+
+  st = d.c_dtype == TB_F16 ? dispatch_tile<__half>(plan, ta, tbm, kp, stream, 1)
+                           : dispatch_tile<float>(plan, ta, tbm, kp, stream, 0);
+  if (st != TB_OK) return st;
+
+  if (plan->epilogue == kEpiWorkspace) {
+    const int64_t plane = d.m * d.n;
+    const int vec = (d.n % 4 == 0) && aligned16(workspace) &&
+                    (reinterpret_cast<uintptr_t>(Cp) % (4 * out_bytes) == 0) &&
+                    ((ldc * (int64_t)out_bytes) % (4 * out_bytes) == 0);
+    const int64_t items = vec ? plane / 4 : plane;
+    int64_t blocks = (items + 255) / 256;
+    const int64_t cap = (int64_t)plan->num_sms * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    if (d.c_dtype == TB_F16)
+      tb_splitk_reduce_kernel<__half><<<(unsigned)blocks, 256, 0, stream>>>(
+          kp.ws, kp.map.split_k, kp.M, kp.N, Cp, ldc, kp.beta, vec);
+    else
+      tb_splitk_reduce_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(
+          kp.ws, kp.map.split_k, kp.M, kp.N, Cp, ldc, kp.beta, vec);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+      return tb_fail(TB_ERR_CUDA, std::string("tb_splitk_reduce launch: ") + cudaGetErrorString(e));
+  }
+  return TB_OK;
+}
+
+extern "C" tbStatus tb_device_status(void* stream, uint32_t* raw) {
+  cudaError_t e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return tb_fail(TB_ERR_CUDA, std::string("cudaStreamSynchronize: ") + cudaGetErrorString(e));
+  uint32_t v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_tb_status, sizeof(v));
+  if (e != cudaSuccess)
+    return tb_fail(TB_ERR_CUDA, std::string("cudaMemcpyFromSymbol: ") + cudaGetErrorString(e));
+  if (raw) *raw = v;
+  if (v != 0) {
+    const uint32_t zero = 0;
+    cudaMemcpyToSymbol(g_tb_status, &zero, sizeof(zero));
+    return tb_fail(TB_ERR_DEVICE_TIMEOUT, "a device-side wait timed out (status 0x" +
+                                              std::to_string(v) + ")");
+  }
+  return TB_OK;
+}

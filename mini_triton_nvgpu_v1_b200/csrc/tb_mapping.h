@@ -1,0 +1,72 @@
+// tb_mapping.h — program-id → work mapping shared by the host plan and the
+// sm_100a kernels. A "program" is the reference's unit of work (one
+// `gpu.func` instance per pid); here resident CTAs walk the program list.
+//
+// The formulas restate the reference's runtime mapping:
+//   * tile / grouped_tile / persistent_tile:
+//       buildProgramWorkAssignment, LowerPipelineToNVGPU.cpp:283-304
+//   * split_k: LowerPipelineToNVGPU.cpp:305-316
+//   * K range of a split part, in block_k tiles:
+//       buildSplitKGroupActivePredicate, LowerPipelineToNVGPU.cpp:325-357
+#pragma once
+
+#include <stdint.h>
+
+#if defined(__CUDACC__)
+#define TB_HD __host__ __device__ __forceinline__
+#else
+#define TB_HD inline
+#endif
+
+namespace tb {
+
+enum MappingKind : int32_t {
+  kMapTile = 0,
+  kMapGroupedTile = 1,
+  kMapSplitK = 2,
+  kMapPersistentTile = 3,
+};
+
+// Plain-old-data copy of the mapping facts the kernels need.
+struct MappingArgs {
+  int32_t kind;
+  int32_t tiles_m, tiles_n, tiles_k;   // problem tiles in block units
+  int32_t group_span_m;                // groupTileSpanM
+  int32_t programs_per_group;          // programsPerLaunchGroup
+  int32_t split_k;
+  int32_t total_programs;
+};
+
+struct Work {
+  int32_t tile_m, tile_n, part;
+  int32_t kt_begin, kt_count;  // K range in block_k tiles
+};
+
+TB_HD Work program_work(const MappingArgs& a, int32_t pid) {
+  Work w;
+  if (a.kind == kMapSplitK) {
+    const int32_t group = pid / a.programs_per_group;
+    const int32_t in_group = pid % a.programs_per_group;
+    w.tile_m = group;
+    w.tile_n = in_group / a.split_k;
+    w.part = in_group % a.split_k;
+    const int32_t base = a.tiles_k / a.split_k;
+    const int32_t extra = a.tiles_k % a.split_k;
+    w.kt_begin = w.part * base + (w.part < extra ? w.part : extra);
+    w.kt_count = base + (w.part < extra ? 1 : 0);
+  } else {
+    const int32_t group = pid / a.programs_per_group;
+    const int32_t first_m = group * a.group_span_m;
+    const int32_t left_m = a.tiles_m - first_m;
+    const int32_t size_m = a.group_span_m < left_m ? a.group_span_m : left_m;
+    const int32_t in_group = pid % a.programs_per_group;
+    w.tile_m = first_m + in_group % size_m;
+    w.tile_n = in_group / size_m;
+    w.part = 0;
+    w.kt_begin = 0;
+    w.kt_count = a.tiles_k;
+  }
+  return w;
+}
+
+}  // namespace tb

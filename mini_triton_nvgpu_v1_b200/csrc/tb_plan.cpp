@@ -1,0 +1,415 @@
+// tb_plan.cpp — knob validation and program mapping behind the C ABI.
+//
+// Host-only C++: the rules and the error messages restate the reference's
+// compile-time analyses so that a knob set the reference rejects is rejected
+// here with the same words:
+//   verifySupportedKernelConfig   lib/Analysis/KernelConfig.cpp:202-246
+//   deriveProgramMappingPlan      lib/Analysis/ProgramMappingPlan.cpp:329-458
+//   validateProgramMappingPlan    lib/Analysis/ProgramMappingPlan.cpp:219-324
+//   deriveReductionPlan           lib/Analysis/ReductionPlan.cpp:137-192
+//   derivePersistentWorkPlan      lib/Analysis/PersistentWorkPlan.cpp:91-131
+//   deriveWarpGrid                lib/Analysis/EncodingPlan.cpp:283-321
+//   selectedMainlineKind          lib/Analysis/ResourceClosurePlan.cpp:154-161
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <limits>
+#include <new>
+#include <sstream>
+#include <string>
+
+#include "tb_plan.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+constexpr int kDefaultB200Sms = 148;
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+const char* dtype_name(int32_t t) {
+  switch (t) {
+    case TB_F16: return "f16";
+    case TB_F32: return "f32";
+    case TB_BF16: return "bf16";
+  }
+  return "?";
+}
+
+// deriveWarpGrid (EncodingPlan.cpp:283-321) for the m16n8k16 instruction
+// shape: the most square warp tile wins; ties prefer more warps along the
+// longer block edge.
+bool derive_warp_grid(int64_t num_warps, int64_t bm, int64_t bn, int64_t* gm,
+                      int64_t* gn) {
+  const int64_t im = 16, in = 8;
+  int64_t best_m = -1, best_n = -1;
+  int64_t best = std::numeric_limits<int64_t>::max();
+  for (int64_t wm = 1; wm <= num_warps; ++wm) {
+    if (num_warps % wm != 0) continue;
+    const int64_t wn = num_warps / wm;
+    if (bm % wm != 0 || bn % wn != 0) continue;
+    const int64_t tm = bm / wm, tn = bn / wn;
+    if (tm % im != 0 || tn % in != 0) continue;
+    const int64_t score = std::llabs(tm - tn);
+    if (score < best || (score == best && ((bm >= bn && wm > best_m) ||
+                                           (bm < bn && wn > best_n)))) {
+      best = score;
+      best_m = wm;
+      best_n = wn;
+    }
+  }
+  if (best_m <= 0 || best_n <= 0) return false;
+  *gm = best_m;
+  *gn = best_n;
+  return true;
+}
+
+}  // namespace
+
+tbStatus tb_fail(tbStatus code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+void tb_clear_error() { g_last_error.clear(); }
+
+extern "C" const char* tb_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" const char* tb_version(void) { return "tbgemm 0.1 (sm_100a tcgen05)"; }
+
+extern "C" tbStatus tb_matmul_desc_init(tb_matmul_desc* d) {
+  if (!d) return tb_fail(TB_ERR_INVALID_ARGUMENT, "desc must not be NULL");
+  std::memset(d, 0, sizeof(*d));
+  d->group_m = 8;         // TBOps.td:45 DefaultValuedAttr<I64Attr, "8">
+  d->exact_tile = 1;      // TBOps.td:46 DefaultValuedAttr<BoolAttr, "true">
+  d->split_k = 1;         // ProgramMappingPlan.cpp:333
+  d->num_ctas = 1;        // ProgramMappingPlan.cpp:331
+  d->persistent = 0;
+  d->programs_per_tile = 0;
+  d->reduction_mode = TB_REDUCTION_UNSET;
+  d->a_dtype = TB_F16;
+  d->b_dtype = TB_F16;
+  d->c_dtype = TB_F32;
+  d->beta = 1;
+  d->num_warps = 4;
+  d->num_stages = 2;
+  return TB_OK;
+}
+
+static tbStatus validate_kernel_config(const tb_matmul_desc& d) {
+  // KernelConfig.cpp:204-207. f16 C is this build's extension.
+  if (d.a_dtype != TB_F16 || d.b_dtype != TB_F16 ||
+      (d.c_dtype != TB_F32 && d.c_dtype != TB_F16))
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "stage1 currently supports fp16 x fp16 -> fp32 matmul kernels");
+  if (d.m <= 0 || d.n <= 0 || d.k <= 0)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "problem M/N/K must be positive");
+  if (d.block_m <= 0 || d.block_n <= 0 || d.block_k <= 0)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "block M/N/K must be positive");
+  if (d.block_m % 16 != 0 || d.block_n % 8 != 0 || d.block_k % 16 != 0)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "stage1 requires block_m % 16 == 0, block_n % 8 == 0 and "
+                   "block_k % 16 == 0 for mma.sync m16n8k16 legality");
+  if (d.num_stages < 2 || d.num_stages > 4)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "stage1 currently supports num_stages in [2, 4]");
+  if (d.num_warps <= 0)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "num_warps must be positive");
+  if (d.group_m <= 0)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "group_m must be positive");
+  if (d.exact_tile && ((d.m % d.block_m) != 0 || (d.n % d.block_n) != 0 ||
+                       (d.k % d.block_k) != 0))
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "exact_tile=true requires problem M/N/K to be divisible by "
+                   "block M/N/K");
+  return TB_OK;
+}
+
+extern "C" tbStatus tb_matmul_plan_create(const tb_matmul_desc* desc, int device,
+                                          tb_matmul_plan** out) {
+  tb_clear_error();
+  if (!desc || !out)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "desc and plan must not be NULL");
+  *out = nullptr;
+  const tb_matmul_desc& d = *desc;
+  tbStatus st = validate_kernel_config(d);
+  if (st != TB_OK) return st;
+
+  int num_sms = kDefaultB200Sms;
+  if (device >= 0) {
+    int n = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess)
+      return tb_fail(TB_ERR_CUDA, std::string("cudaDeviceGetAttribute: ") +
+                                      cudaGetErrorString(e));
+    num_sms = n;
+  }
+
+  tb_matmul_plan p;
+  p.desc = d;
+  p.device = device;
+  p.num_sms = num_sms;
+
+  // ---- deriveProgramMappingPlan (ProgramMappingPlan.cpp:329-458) ----
+  const int64_t tiles_m = ceil_div(d.m, d.block_m);
+  const int64_t tiles_n = ceil_div(d.n, d.block_n);
+  const int64_t tiles_k = ceil_div(d.k, d.block_k);
+  int64_t group_m = std::max<int64_t>(1, d.group_m);
+  int64_t span_m = 1, span_n = tiles_n;
+  int64_t ppg = span_m * span_n;
+  int64_t launch_groups = tiles_m;
+  int64_t total = tiles_m * tiles_n;
+  const int64_t split_k = std::max<int64_t>(d.split_k, 1);  // :361
+  int64_t num_ctas = d.num_ctas;
+  int64_t programs_per_tile = 1;
+
+  if (d.persistent && split_k != 1)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "stage1 does not allow persistent and split-k in the same "
+                   "program mapping contract yet");
+  if (num_ctas <= 0)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "module attr `tb.num-ctas` must be positive");
+  if (d.programs_per_tile > 0) programs_per_tile = d.programs_per_tile;
+  if (d.reduction_mode != TB_REDUCTION_UNSET &&
+      d.reduction_mode != TB_REDUCTION_SPLIT_K_SERIAL &&
+      d.reduction_mode != TB_REDUCTION_SPLIT_K_PARALLEL)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "module attr `tb.reduction-mode` must be `split_k_serial` or "
+                   "`split_k_parallel`");
+
+  int32_t kind;
+  std::string reduction = "none";
+  if (d.persistent) {
+    kind = tb::kMapPersistentTile;
+    p.mapping_kind = "persistent_tile";
+    p.launch_order = "persistent";
+    p.swizzle_kind = "none";
+    group_m = 1;
+    span_m = 1;
+    span_n = tiles_n;
+    ppg = span_n;
+    launch_groups = tiles_m;
+    total = tiles_m * tiles_n;
+    programs_per_tile = 1;
+    num_ctas = std::min<int64_t>(num_ctas, total);
+  } else if (split_k > 1) {
+    kind = tb::kMapSplitK;
+    p.mapping_kind = "split_k";
+    p.launch_order = "row_major";
+    p.swizzle_kind = "none";
+    group_m = 1;
+    span_m = 1;
+    span_n = tiles_n * split_k;
+    ppg = span_n;
+    launch_groups = tiles_m;
+    total = tiles_m * tiles_n * split_k;
+    programs_per_tile = split_k;
+    if (d.reduction_mode == TB_REDUCTION_SPLIT_K_PARALLEL)
+      reduction = "split_k_atomic";      // ReductionPlan.cpp:176-182
+    else
+      reduction = "split_k_serial";      // ReductionPlan.cpp:169-175
+  } else if (group_m > 1 && tiles_m > 1 && tiles_n > 1) {
+    kind = tb::kMapGroupedTile;
+    p.mapping_kind = "grouped_tile";
+    p.launch_order = "grouped_m";
+    p.swizzle_kind = "grouped_m";
+    span_m = group_m;
+    span_n = tiles_n;
+    ppg = span_m * span_n;
+    launch_groups = ceil_div(tiles_m, group_m);
+    total = tiles_m * tiles_n;
+  } else {
+    kind = tb::kMapTile;
+    p.mapping_kind = "tile";
+    p.launch_order = "row_major";
+    p.swizzle_kind = "none";
+    group_m = 1;
+    span_m = 1;
+    span_n = tiles_n;
+    ppg = span_n;
+    launch_groups = tiles_m;
+    total = tiles_m * tiles_n;
+  }
+  if (d.persistent && num_ctas > num_sms) num_ctas = num_sms;  // :450-453
+
+  if (total > std::numeric_limits<int32_t>::max() ||
+      tiles_k > std::numeric_limits<int32_t>::max())
+    return tb_fail(TB_ERR_UNSUPPORTED, "program count exceeds 2^31-1");
+
+  // deriveWarpGrid failure is a layout-plan error in the reference.
+  int64_t wgm = 0, wgn = 0;
+  if (!derive_warp_grid(d.num_warps, d.block_m, d.block_n, &wgm, &wgn))
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "failed to derive a legal warp grid from module num-warps, "
+                   "block shape and mma instruction shape");
+
+  p.map.kind = kind;
+  p.map.tiles_m = (int32_t)tiles_m;
+  p.map.tiles_n = (int32_t)tiles_n;
+  p.map.tiles_k = (int32_t)tiles_k;
+  p.map.group_span_m = (int32_t)span_m;
+  p.map.programs_per_group = (int32_t)ppg;
+  p.map.split_k = (int32_t)split_k;
+  p.map.total_programs = (int32_t)total;
+  p.reduction_kind = reduction;
+  p.launch_group_count = launch_groups;
+  p.group_tile_span_n = span_n;
+  p.programs_per_tile = programs_per_tile;
+  p.num_ctas = num_ctas;
+  p.resident_programs = d.persistent ? std::max<int64_t>(1, std::min<int64_t>(num_ctas, num_sms)) : 1;
+  p.warp_grid_m = wgm;
+  p.warp_grid_n = wgn;
+  if (d.persistent) p.mainline_kind = "persistent_tile_loop";
+  else if (split_k > 1) p.mainline_kind = "split_k";
+  else if (kind == tb::kMapGroupedTile) p.mainline_kind = "grouped_tile";
+  else p.mainline_kind = "single_tile";
+
+  // ---- this build's hardware tile (tcgen05 M=128, N ∈ {64,128,256}) ----
+  if (d.block_m > 128)
+    return tb_fail(TB_ERR_UNSUPPORTED,
+                   "block_m > 128 is not supported by the sm_100a kernels of "
+                   "this build (one tcgen05 M=128 accumulator per program)");
+  if (d.block_n > 256)
+    return tb_fail(TB_ERR_UNSUPPORTED,
+                   "block_n > 256 is not supported (tcgen05 N <= 256)");
+  p.cta_m = 128;
+  if (d.block_n <= 64) { p.kernel_tile = kTile128x64; p.cta_n = 64; }
+  else if (d.block_n <= 128) { p.kernel_tile = kTile128x128; p.cta_n = 128; }
+  else { p.kernel_tile = kTile128x256; p.cta_n = 256; }
+  // The ring is as deep as shared memory allows and never shallower than
+  // tb.requested-stages.
+  p.stages = std::max<int32_t>((int32_t)d.num_stages, tb_kernel_max_stages(p.kernel_tile));
+  p.smem_bytes = tb_kernel_smem_bytes(p.kernel_tile, p.stages);
+  p.tmem_cols = 2 * p.cta_n;  // two accumulators (epilogue/mainloop overlap)
+
+  if (split_k > 1) {
+    if (d.reduction_mode == TB_REDUCTION_SPLIT_K_PARALLEL) {
+      if (d.c_dtype != TB_F32)
+        return tb_fail(TB_ERR_UNSUPPORTED,
+                       "split_k_parallel accumulates with f32 atomics; f16 C "
+                       "needs split_k_serial");
+      p.epilogue = kEpiAtomic;
+      p.workspace_bytes = 0;
+    } else {
+      p.epilogue = kEpiWorkspace;
+      p.workspace_bytes = (size_t)split_k * (size_t)d.m * (size_t)d.n * sizeof(float);
+    }
+  } else {
+    p.epilogue = kEpiStore;
+    p.workspace_bytes = 0;
+  }
+  const int64_t want = d.persistent ? p.resident_programs : total;
+  p.grid = std::max<int64_t>(1, std::min<int64_t>(want, num_sms));
+
+  tb_matmul_plan* heap = new (std::nothrow) tb_matmul_plan(p);
+  if (!heap) return tb_fail(TB_ERR_INVALID_ARGUMENT, "out of host memory");
+  *out = heap;
+  return TB_OK;
+}
+
+extern "C" tbStatus tb_matmul_plan_destroy(tb_matmul_plan* plan) {
+  delete plan;
+  return TB_OK;
+}
+
+extern "C" size_t tb_matmul_workspace_bytes(const tb_matmul_plan* plan) {
+  return plan ? plan->workspace_bytes : 0;
+}
+
+extern "C" tbStatus tb_matmul_program_work(const tb_matmul_plan* plan, int64_t pid,
+                                           tb_program_work* w) {
+  if (!plan || !w) return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan and work must not be NULL");
+  if (pid < 0 || pid >= plan->map.total_programs)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "program id out of range");
+  const tb::Work x = tb::program_work(plan->map, (int32_t)pid);
+  w->tile_m = x.tile_m;
+  w->tile_n = x.tile_n;
+  w->split_part = x.part;
+  w->k_tile_begin = x.kt_begin;
+  w->k_tile_count = x.kt_count;
+  return TB_OK;
+}
+
+extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* buf,
+                                            size_t len, size_t* needed) {
+  if (!plan) return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan must not be NULL");
+  const tb_matmul_desc& d = plan->desc;
+  const char* kernel_names[] = {"tb_gemm_sm100_128x64", "tb_gemm_sm100_128x128",
+                                "tb_gemm_sm100_128x256"};
+  const char* epi_names[] = {"store", "workspace_partial", "atomic_add"};
+  std::ostringstream o;
+  o << "{";
+  o << "\"problem\": [" << d.m << ", " << d.n << ", " << d.k << "], ";
+  o << "\"tile\": [" << d.block_m << ", " << d.block_n << ", " << d.block_k << "], ";
+  o << "\"dtypes\": \"" << dtype_name(d.a_dtype) << "x" << dtype_name(d.b_dtype)
+    << "->" << dtype_name(d.c_dtype) << "\", ";
+  o << "\"exact_tile\": " << (d.exact_tile ? "true" : "false") << ", ";
+  o << "\"num_warps\": " << d.num_warps << ", ";
+  o << "\"requested_stages\": " << d.num_stages << ", ";
+  o << "\"warp_grid\": [" << plan->warp_grid_m << ", " << plan->warp_grid_n << "], ";
+  o << "\"mapping_kind\": \"" << plan->mapping_kind << "\", ";
+  o << "\"launch_order\": \"" << plan->launch_order << "\", ";
+  o << "\"swizzle_kind\": \"" << plan->swizzle_kind << "\", ";
+  o << "\"problem_tiles\": [" << plan->map.tiles_m << ", " << plan->map.tiles_n
+    << ", " << plan->map.tiles_k << "], ";
+  o << "\"group_m\": " << (plan->map.kind == tb::kMapGroupedTile ? plan->map.group_span_m : 1) << ", ";
+  o << "\"group_tile_span_m\": " << plan->map.group_span_m << ", ";
+  o << "\"group_tile_span_n\": " << plan->group_tile_span_n << ", ";
+  o << "\"programs_per_launch_group\": " << plan->map.programs_per_group << ", ";
+  o << "\"launch_group_count\": " << plan->launch_group_count << ", ";
+  o << "\"total_programs\": " << plan->map.total_programs << ", ";
+  o << "\"split_k\": " << plan->map.split_k << ", ";
+  o << "\"programs_per_tile\": " << plan->programs_per_tile << ", ";
+  o << "\"reduction_kind\": \"" << plan->reduction_kind << "\", ";
+  o << "\"persistent\": " << (d.persistent ? "true" : "false") << ", ";
+  o << "\"persistent_kind\": \"" << (d.persistent ? "tile_stride_loop" : "none") << "\", ";
+  o << "\"num_ctas\": " << plan->num_ctas << ", ";
+  o << "\"resident_programs\": " << plan->resident_programs << ", ";
+  o << "\"selected_mainline_kind\": \"" << plan->mainline_kind << "\", ";
+  o << "\"num_sms\": " << plan->num_sms << ", ";
+  o << "\"kernel\": \"" << kernel_names[plan->kernel_tile] << "\", ";
+  o << "\"cta_tile\": [" << plan->cta_m << ", " << plan->cta_n << ", 64], ";
+  o << "\"stages\": " << plan->stages << ", ";
+  o << "\"smem_bytes\": " << plan->smem_bytes << ", ";
+  o << "\"tmem_cols\": " << plan->tmem_cols << ", ";
+  o << "\"grid\": " << plan->grid << ", ";
+  o << "\"block_threads\": 192, ";
+  o << "\"epilogue\": \"" << epi_names[plan->epilogue] << "\", ";
+  o << "\"beta\": " << d.beta << ", ";
+  o << "\"workspace_bytes\": " << plan->workspace_bytes;
+  o << "}";
+  const std::string s = o.str();
+  if (needed) *needed = s.size() + 1;
+  if (!buf || len < s.size() + 1)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "describe buffer too small");
+  std::memcpy(buf, s.c_str(), s.size() + 1);
+  return TB_OK;
+}
+
+extern "C" tbStatus tb_matmul_run(const tb_matmul_plan* plan, const void* A, int64_t lda,
+                                  const void* B, int64_t ldb, void* C, int64_t ldc,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  tb_clear_error();
+  if (!plan) return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan must not be NULL");
+  return tb_launch(plan, A, lda, B, ldb, C, ldc, workspace, workspace_bytes, stream);
+}
+
+extern "C" tbStatus tb_matmul(const tb_matmul_desc* desc, const void* A, int64_t lda,
+                              const void* B, int64_t ldb, void* C, int64_t ldc,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return tb_fail(TB_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  tb_matmul_plan* plan = nullptr;
+  tbStatus st = tb_matmul_plan_create(desc, dev, &plan);
+  if (st != TB_OK) return st;
+  st = tb_matmul_run(plan, A, lda, B, ldb, C, ldc, workspace, workspace_bytes, stream);
+  tb_matmul_plan_destroy(plan);
+  return st;
+}

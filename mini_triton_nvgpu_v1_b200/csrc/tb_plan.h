@@ -1,0 +1,66 @@
+// tb_plan.h — the immutable plan behind the C ABI's opaque tb_matmul_plan.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/tb_gemm.h"
+#include "tb_mapping.h"
+
+// Kernel family selected by the plan (the hardware CTA tile; the program tile
+// is block_m × block_n and may be smaller, with the rest masked).
+enum TbKernelTile : int32_t {
+  kTile128x64 = 0,
+  kTile128x128 = 1,
+  kTile128x256 = 2,
+};
+
+enum TbEpilogue : int32_t {
+  kEpiStore = 0,      // C = beta·C_in + acc
+  kEpiWorkspace = 1,  // ws[part] = acc   (split_k_serial)
+  kEpiAtomic = 2,     // C += acc atomically (split_k_parallel)
+};
+
+struct tb_matmul_plan {
+  tb_matmul_desc desc;
+  int device;
+  int num_sms;
+
+  // --- reference plan facts (ProgramMappingPlan / ReductionPlan /
+  //     PersistentWorkPlan / EncodingPlan) ---
+  tb::MappingArgs map;
+  std::string mapping_kind;    // "tile" | "grouped_tile" | "split_k" | "persistent_tile"
+  std::string launch_order;    // "row_major" | "grouped_m" | "persistent"
+  std::string swizzle_kind;    // "none" | "grouped_m"
+  std::string reduction_kind;  // "none" | "split_k_serial" | "split_k_atomic"
+  std::string mainline_kind;   // "single_tile" | "grouped_tile" | "split_k" | "persistent_tile_loop"
+  int64_t launch_group_count;
+  int64_t group_tile_span_n;
+  int64_t programs_per_tile;
+  int64_t num_ctas;            // after the reference's clamps
+  int64_t resident_programs;   // persistent: min(num_ctas, numSms)
+  int64_t warp_grid_m, warp_grid_n;
+
+  // --- this build's launch facts ---
+  int32_t kernel_tile;         // TbKernelTile
+  int32_t cta_m, cta_n;        // hardware tile
+  int32_t stages;              // shared-memory ring depth (64-deep K stages)
+  int32_t epilogue;            // TbEpilogue
+  int64_t grid;                // CTAs launched
+  size_t smem_bytes;
+  int32_t tmem_cols;
+  size_t workspace_bytes;
+};
+
+// Defined in tb_launch.cu.
+tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda,
+                   const void* B, int64_t ldb, void* C, int64_t ldc,
+                   void* workspace, size_t workspace_bytes, void* stream);
+size_t tb_kernel_smem_bytes(int32_t kernel_tile, int32_t stages);
+int32_t tb_kernel_max_stages(int32_t kernel_tile);
+
+// Thread-local error message helpers (tb_plan.cpp).
+tbStatus tb_fail(tbStatus code, const std::string& msg);
+void tb_clear_error();
