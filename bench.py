@@ -1,0 +1,347 @@
+#!/usr/bin/env python3
+"""bench.py — TFLOP/s of the B200-native `tb.matmul` at 8192³ f16→f32.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one tb.matmul (C ← C_in + A·B, f16 A/B, f32 C) of the per-GPU
+problem 8192 × 8192 × 8192 with GROUP_M=8 program swizzle (the BASELINE
+"Grouped-M swizzle" config). With N GPUs the global problem is
+8192 × (8192·N) × 8192 sharded along N columns — each rank holds A and its
+own B/C column slice, no collective (weak scaling). Inputs are seeded
+synthetic N(0,1)·0.1 f16; A+B+C = 512 MiB per GPU, larger than the 126 MB L2,
+so no flush is needed between steps.
+
+JSON keys: value = whole-job TFLOP/s with inputs resident in HBM (CUDA
+events, max over ranks); e2e = the same through the public API with the
+step's inputs copied from pinned host memory and C copied back inside the
+timed region; roofline = the GEMM kernel's achieved TFLOP/s against the
+measured cuBLAS bf16 peak; cpu_baseline = the CPU oracle on the host cores.
+
+--impl reference times the reference's CPU path for tb.matmul on the host
+cores: the reference itself cannot be built here (it is an MLIR dialect and
+needs an LLVM/MLIR toolchain this image lacks), so its semantics are run
+through the C restatement in oracle/ (kind "port") with every host thread.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GEMM TFLOP/s & % of B200 dense f16 peak at 8192^3 f16->f32"
+M = N_PER_GPU = K = 8192
+BLOCK = dict(block_m=256, block_n=256, block_k=64, group_m=8, num_warps=4, num_stages=4)
+FALLBACK_PEAK_TFLOPS = 1590.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", FALLBACK_PEAK_TFLOPS), d.get("bf16_tflops_sustained"), "measured"
+    return FALLBACK_PEAK_TFLOPS, 1400.0, "fallback"
+
+
+def traffic_for(kernel: str):
+    """DRAM bytes per launch of `kernel` on this workload, from the committed
+    ncu summary (profiles/traffic.json); None when not captured."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    e = d.get(f"{kernel} {M}x{N_PER_GPU}x{K}")
+    return None if e is None else e.get("dram_bytes_per_launch")
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons of one GPU, sampled every
+    200 ms while running."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, phys_index: int):
+        self.idx = phys_index
+        self.rows = []
+        self.proc = None
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        if not self.rows:
+            return None
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def phys_gpu_index(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if local < len(ids) and ids[local].isdigit():
+            return int(ids[local])
+    return local
+
+
+_CPU_INPUTS = {}
+
+
+def cpu_sample(rows: int, threads: int = 0, seed: int = 4):
+    """Times the CPU oracle on `rows` rows of the 8192³ problem (same K, N;
+    inputs generated once, outside the timing). Returns (seconds, flops)."""
+    import numpy as np
+    import oracle
+    if "B" not in _CPU_INPUTS:
+        rng = np.random.default_rng(seed)
+        _CPU_INPUTS["B"] = (rng.standard_normal((K, N_PER_GPU), dtype=np.float32) * 0.1).astype(np.float16)
+        _CPU_INPUTS["A"] = (rng.standard_normal((M, K), dtype=np.float32) * 0.1).astype(np.float16)
+    A = _CPU_INPUTS["A"][:rows]
+    B = _CPU_INPUTS["B"]
+    C = np.zeros((rows, N_PER_GPU), np.float32)
+    t0 = time.perf_counter()
+    oracle.matmul_ref(A, B, C, threads=threads)
+    return time.perf_counter() - t0, 2.0 * rows * N_PER_GPU * K
+
+
+def cpu_baseline_block(budget_s: float = 10.0):
+    import oracle
+    threads = oracle.max_threads()
+    dt, fl = cpu_sample(64, threads)
+    rate = fl / dt
+    rows = int(max(64, min(M, (budget_s * rate) / (2.0 * N_PER_GPU * K))) // 64 * 64)
+    dt, fl = cpu_sample(rows, threads)
+    return {"value": round(fl / dt / 1e12, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {M} rows of the {M}x{N_PER_GPU}x{K} problem (C_in + A·B, f16->f32), "
+                      f"{dt:.1f} s, oracle/tb_oracle.c with {threads} POSIX threads"}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    import oracle
+    threads = oracle.max_threads()
+    steps, warm = max(1, args.steps), max(0, args.warmup)
+    dt, fl = cpu_sample(64, threads)
+    per_step_budget = min(10.0, 150.0 / (steps + warm))
+    rows = int(max(16, min(M, per_step_budget * (fl / dt) / (2.0 * N_PER_GPU * K))) // 16 * 16)
+    for _ in range(warm):
+        cpu_sample(rows, threads)
+    total_t, total_f = 0.0, 0.0
+    for _ in range(steps):
+        t, f = cpu_sample(rows, threads)
+        total_t += t
+        total_f += f
+    value = total_f / total_t / 1e12
+    sample = (f"{rows} of {M} rows of the {M}x{N_PER_GPU}x{K} tb.matmul per step (reference semantics "
+              f"through oracle/tb_oracle.c; the MLIR reference needs an LLVM/MLIR toolchain absent here)")
+    out = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": warm,
+        "ms_per_step": round(1e3 * total_t / steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"tb.matmul {M}x{N_PER_GPU}x{K} f16->f32 (CPU sample per step)",
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import mini_triton_nvgpu_v1_b200 as tb
+
+    rank, world, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+
+    # Per-rank shard: A replicated, B/C column slice `rank` of the global N.
+    g = torch.Generator(device=dev).manual_seed(4)
+    A = (torch.randn(M, K, device=dev, generator=g) * 0.1).half()
+    g.manual_seed(1000 + rank)
+    B = (torch.randn(K, N_PER_GPU, device=dev, generator=g) * 0.1).half()
+    Cm = torch.zeros(M, N_PER_GPU, device=dev, dtype=torch.float32)
+
+    cfg = tb.KernelConfig(m=M, n=N_PER_GPU, k=K, **BLOCK)
+    plan = tb.MatmulPlan(cfg, local)
+    info = plan.info
+    launches_per_step = 1 + (1 if info["epilogue"] == "workspace_partial" else 0)
+
+    def step():
+        plan.run_ptr(A.data_ptr(), K, B.data_ptr(), N_PER_GPU, Cm.data_ptr(), N_PER_GPU, 0, 0,
+                     stream.cuda_stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    tb.device_status(stream)
+
+    sampler = ClockSampler(phys_gpu_index(local))
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_step = ms_max / args.steps
+    flops_step_rank = 2.0 * M * N_PER_GPU * K
+    value = flops_step_rank * world / (ms_step * 1e-3) / 1e12
+    tb.device_status(stream)
+
+    # ---- e2e: public API, inputs from pinned host memory, result read back ----
+    hA = A.cpu().pin_memory()
+    hB = B.cpu().pin_memory()
+    hC = torch.zeros(M, N_PER_GPU, dtype=torch.float32).pin_memory()
+    hOut = torch.empty(M, N_PER_GPU, dtype=torch.float32).pin_memory()
+    dA, dB, dC = torch.empty_like(A), torch.empty_like(B), torch.empty_like(Cm)
+
+    def e2e_step():
+        dA.copy_(hA, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        dC.copy_(hC, non_blocking=True)
+        tb.matmul(dA, dB, dC, **BLOCK)
+        hOut.copy_(dC, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item()) / args.e2e_steps
+    e2e_value = flops_step_rank * world / (e2e_ms * 1e-3) / 1e12
+    h2d = A.numel() * 2 + B.numel() * 2 + Cm.numel() * 4
+    d2h = Cm.numel() * 4
+
+    if rank == 0:
+        peak, peak_sus, peak_src = peaks()
+        achieved = flops_step_rank / (ms_step * 1e-3) / 1e12  # one launch per step on this config
+        kern = info["kernel"]
+        cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline_block()
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic",
+            "config": {"workload": f"tb.matmul {M}x{N_PER_GPU * world}x{K} f16->f32 C+=A·B, "
+                                   f"N-sharded {N_PER_GPU} columns per GPU, GROUP_M=8",
+                       "m": M, "n_per_gpu": N_PER_GPU, "k": K, **{k: v for k, v in BLOCK.items()},
+                       "kernel": kern, "grid": info["grid"], "stages": info["stages"],
+                       "l2": "inputs larger than L2 (512 MiB per GPU), no flush",
+                       "parallelism": f"N-shard x{world}, no collective"},
+            "pct_of_peak": round(100.0 * value / world / peak, 2),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_src} bf16 burst",
+                         "frac_of_sustained": round(achieved / peak_sus, 4) if peak_sus else None,
+                         "traffic": traffic_for(kern),
+                         "algorithmic_bytes": 2 * (M * K + K * N_PER_GPU) + 8 * M * N_PER_GPU},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 3),
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "mini_triton_nvgpu_v1_b200.matmul"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

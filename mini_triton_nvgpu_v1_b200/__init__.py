@@ -119,8 +119,9 @@ class MatmulPlan:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h is not None and h.value:
-            _lib.tb_matmul_plan_destroy(h)
+        lib_ = _lib  # may already be None during interpreter shutdown
+        if h is not None and h.value and lib_ is not None:
+            lib_.tb_matmul_plan_destroy(h)
             self._h = C.c_void_p()
 
     def _describe(self) -> dict:

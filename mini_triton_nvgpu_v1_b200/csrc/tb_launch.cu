@@ -44,6 +44,16 @@ using namespace tb::sm100;
 
 __device__ uint32_t g_tb_status = 0;
 
+#ifdef TB_WAIT_PROFILE
+// Debug builds only: cycles each role spent in bounded waits, summed over CTAs.
+// [0] producer/empty [1] mma/full [2] mma/tempty [3] epilogue/tfull
+// [4] kernel cycles (per CTA, summed) [5] epilogue busy cycles
+__device__ unsigned long long g_tb_prof[8];
+#define TB_PROF_ADD(i, v) atomicAdd(&g_tb_prof[i], (unsigned long long)(v))
+#else
+#define TB_PROF_ADD(i, v) ((void)0)
+#endif
+
 namespace {
 
 constexpr int kThreads = 192;
@@ -56,14 +66,20 @@ constexpr long long kWaitBudgetCycles = 2000000000LL;  // ≈1 s at 1.9 GHz
 
 constexpr uint32_t kSiteProducer = 1, kSiteMma = 2, kSiteEpilogue = 3, kSiteDrain = 4;
 
-template <int BN>
+// G = CTAs per tile: 1 (cta_group::1, 128-row tile) or 2 (cta_group::2 pair,
+// 256-row tile; each CTA holds 128 rows of A, BN/2 columns of B and 128
+// rows of the accumulator).
+template <int BN, int G>
 struct Cfg {
-  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr int kBnCta = BN / G;                  // B columns per CTA
+  static constexpr uint32_t kBBytes = kBnCta * kBK * 2;  // kBnCta/64 boxes
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr int kRawStages = (int)((kSmemLimit - 1024 - 512) / kStageBytes);
   static constexpr int kStages = kRawStages > 8 ? 8 : kRawStages;
-  static constexpr uint32_t kTmemCols = 2 * BN;  // 128, 256 or 512: powers of two
+  static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators of BN f32 columns
   static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 512;
+  static_assert(kBnCta % 64 == 0, "B columns per CTA must be whole 64-column boxes");
+  static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512, "TMEM columns");
 };
 
 struct KParams {
@@ -100,6 +116,28 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+// wait_bounded plus (debug builds) the cycles spent waiting, added to slot.
+__device__ __forceinline__ bool wait_prof(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          uint32_t site, int slot, long long& acc) {
+#ifdef TB_WAIT_PROFILE
+  const long long t0 = clock64();
+  const bool r = wait_bounded(bar, parity, abort_flag, site);
+  acc += clock64() - t0;
+  return r;
+#else
+  (void)slot; (void)acc;
+  return wait_bounded(bar, parity, abort_flag, site);
+#endif
+}
+
+// Lane 0 waits (bounded), the result is broadcast so the warp stays converged.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          uint32_t site, int lane, long long& acc) {
+  int ok = 0;
+  if (lane == 0) ok = wait_prof(bar, parity, abort_flag, site, 0, acc);
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 struct Extent {
   int32_t m0, n0, rows, cols, k_begin, k_end, nkb, part;
 };
@@ -121,35 +159,42 @@ __device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pid) 
 template <typename OutT>
 struct OutIO;
 
+// C is touched once per tile: loads and stores use the streaming (evict-first)
+// cache policy so they do not push reusable A/B lines out of L2.
 template <>
 struct OutIO<float> {
-  static __device__ __forceinline__ float load(const float* p) { return *p; }
-  static __device__ __forceinline__ void store(float* p, float v) { *p = v; }
+  static __device__ __forceinline__ float load(const float* p) { return __ldcs(p); }
+  static __device__ __forceinline__ void store(float* p, float v) { __stcs(p, v); }
   // 32 consecutive values, 16-byte aligned.
   static __device__ __forceinline__ void load32(const float* p, float (&c)[32]) {
     const float4* q = reinterpret_cast<const float4*>(p);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float4 t = q[i];
+      const float4 t = __ldcs(q + i);
       c[4 * i] = t.x; c[4 * i + 1] = t.y; c[4 * i + 2] = t.z; c[4 * i + 3] = t.w;
     }
   }
   static __device__ __forceinline__ void store32(float* p, const float (&v)[32]) {
     float4* q = reinterpret_cast<float4*>(p);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    for (int i = 0; i < 8; ++i) __stcs(q + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
   }
 };
 
 template <>
 struct OutIO<__half> {
-  static __device__ __forceinline__ float load(const __half* p) { return __half2float(*p); }
-  static __device__ __forceinline__ void store(__half* p, float v) { *p = __float2half_rn(v); }
+  static __device__ __forceinline__ float load(const __half* p) {
+    const unsigned short u = __ldcs(reinterpret_cast<const unsigned short*>(p));
+    return __half2float(__ushort_as_half(u));
+  }
+  static __device__ __forceinline__ void store(__half* p, float v) {
+    __stcs(reinterpret_cast<unsigned short*>(p), __half_as_ushort(__float2half_rn(v)));
+  }
   static __device__ __forceinline__ void load32(const __half* p, float (&c)[32]) {
     const uint4* q = reinterpret_cast<const uint4*>(p);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint4 t = q[i];
+      const uint4 t = __ldcs(q + i);
       const uint32_t w[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -170,33 +215,40 @@ struct OutIO<__half> {
         const __half2 h = __floats2half2_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
         w[j] = *reinterpret_cast<const uint32_t*>(&h);
       }
-      q[i] = make_uint4(w[0], w[1], w[2], w[3]);
+      __stcs(q + i, make_uint4(w[0], w[1], w[2], w[3]));
     }
   }
 };
 
-template <int BN, typename OutT>
+template <int BN, int G, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     tb_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB, const KParams p) {
-  using C = Cfg<BN>;
-  constexpr int S = C::kStages;
+  using Cf = Cfg<BN, G>;
+  constexpr int S = Cf::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + (size_t)S * kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)S * C::kBBytes);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + S;
-  uint64_t* tfull = bars + 2 * S;
-  uint64_t* tempty = bars + 2 * S + 2;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)S * Cf::kBBytes);
+  uint64_t* full = bars;            // leader: A/B of both CTAs landed
+  uint64_t* empty = bars + S;       // every CTA: stage consumed by the MMAs
+  uint64_t* tfull = bars + 2 * S;   // every CTA: accumulator ready
+  uint64_t* tempty = bars + 2 * S + 2;  // leader: accumulator drained by all epilogues
   uint64_t* drain = bars + 2 * S + 4;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
+#ifdef TB_WAIT_PROFILE
+  const long long kernel_t0 = clock64();
+#endif
   const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
   const int lane = threadIdx.x % 32;
+  const uint32_t rank = (G == 2) ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int32_t first_pid = blockIdx.x / G;
+  const int32_t pid_stride = gridDim.x / G;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -205,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_addr(&tfull[a]), 1);
-      mbar_init(smem_addr(&tempty[a]), 4);
+      mbar_init(smem_addr(&tempty[a]), 4 * G);
     }
     mbar_init(smem_addr(drain), 1);
     *abort_flag = 0;
@@ -214,112 +266,181 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(smem_addr(tmem_holder), C::kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_g<G>(smem_addr(tmem_holder), Cf::kTmemCols);
+    tmem_relinquish_g<G>();
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (G == 2) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      long long issued = 0;
-      for (int32_t pid = blockIdx.x; pid < p.map.total_programs; pid += gridDim.x) {
-        const Extent e = program_extent(p, pid);
-        bool ok = true;
-        for (int kb = 0; kb < e.nkb; ++kb) {
-          if (!wait_bounded(smem_addr(&empty[stage]), phase ^ 1u, abort_flag, kSiteProducer)) {
-            ok = false;
-            break;
-          }
-          const uint32_t fb = smem_addr(&full[stage]);
-          mbar_expect_tx(fb, C::kStageBytes);
-          const int32_t kx = e.k_begin + kb * kBK;
-          tma_load_2d(smem_addr(sA + (size_t)stage * kABytes), &tmA, fb, kx, e.m0);
+    // The whole warp runs the loop (warp-uniform values live in uniform
+    // registers); one elected lane issues the TMA copies.
+    int stage = 0;
+    uint32_t phase = 0;
+    long long issued = 0;
+    long long prof_w = 0;
+    for (int32_t pid = first_pid; pid < p.map.total_programs; pid += pid_stride) {
+      const Extent e = program_extent(p, pid);
+      bool ok = true;
+      for (int kb = 0; kb < e.nkb; ++kb) {
+        if (!warp_wait(smem_addr(&empty[stage]), phase ^ 1u, abort_flag, kSiteProducer, lane, prof_w)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb_local = smem_addr(&full[stage]);
+#ifdef TB_DEBUG_NO_LOADS
+        // Debug builds only: measure the MMA issue rate without operand traffic.
+        if (leader && elect_one()) mbar_arrive(fb_local);
+        __syncwarp();
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+        continue;
+#endif
+        const int32_t kx = e.k_begin + kb * kBK;
+        const uint32_t dA = smem_addr(sA + (size_t)stage * kABytes);
+        const uint32_t dB = smem_addr(sB + (size_t)stage * Cf::kBBytes);
+        if (elect_one()) {
+          if (leader) mbar_expect_tx(fb_local, G * Cf::kStageBytes);
+          if constexpr (G == 2) {
+            const uint32_t fb = map_to_cta(fb_local, 0);
+            tma_load_2d_pair(dA, &tmA, fb, kx, e.m0 + (int32_t)rank * 128);
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(smem_addr(sB + (size_t)stage * C::kBBytes + (size_t)j * kBBoxBytes), &tmB, fb,
-                        e.n0 + 64 * j, kx);
-          ++issued;
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1u;
+            for (int j = 0; j < Cf::kBnCta / 64; ++j)
+              tma_load_2d_pair(dB + j * kBBoxBytes, &tmB, fb, e.n0 + (int32_t)rank * Cf::kBnCta + 64 * j,
+                               kx);
+          } else {
+            tma_load_2d(dA, &tmA, fb_local, kx, e.m0);
+#pragma unroll
+            for (int j = 0; j < Cf::kBnCta / 64; ++j)
+              tma_load_2d(dB + j * kBBoxBytes, &tmB, fb_local, e.n0 + 64 * j, kx);
           }
         }
-        if (!ok) break;
+        __syncwarp();
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
-      // Drain: the newest fill of each stage must land before the CTA exits.
-      const long long last = issued < S ? issued : S;
-      for (long long i = 0; i < last; ++i) {
-        const long long f = issued - 1 - i;
-        const int s = (int)(f % S);
-        const uint32_t par = (uint32_t)((f / S) & 1);
-        const long long t0 = clock64();
-        while (!mbar_try_wait(smem_addr(&full[s]), par)) {
-          if (clock64() - t0 > kWaitBudgetCycles) {
-            record_error(TB_ERR_DEVICE_TIMEOUT, kSiteDrain);
-            break;
+      if (!ok) break;
+    }
+    if (lane == 0) {
+      TB_PROF_ADD(0, prof_w);
+      // Drain: the newest fill of each stage must land before the CTA exits
+      // (only the leader's full barriers count the bytes).
+      if (leader) {
+        const long long last = issued < S ? issued : S;
+        for (long long i = 0; i < last; ++i) {
+          const long long f = issued - 1 - i;
+          const int s = (int)(f % S);
+          const uint32_t par = (uint32_t)((f / S) & 1);
+          const long long t0 = clock64();
+          while (!mbar_try_wait(smem_addr(&full[s]), par)) {
+            if (clock64() - t0 > kWaitBudgetCycles) {
+              record_error(TB_ERR_DEVICE_TIMEOUT, kSiteDrain);
+              break;
+            }
           }
         }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(kCtaM, BN, 0, 1);
+    // Leader CTA only. Whole warp runs the loop; descriptors are computed
+    // warp-uniformly and one elected lane issues tcgen05.mma / commit.
+    if (leader) {
+      constexpr uint32_t idesc = idesc_f16_f32(kCtaM * G, BN, 0, 1);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool issued_any = false;
       bool ok = true;
-      for (int32_t pid = blockIdx.x; pid < p.map.total_programs && ok; pid += gridDim.x) {
+      long long prof_full = 0, prof_te = 0;
+      for (int32_t pid = first_pid; pid < p.map.total_programs && ok; pid += pid_stride) {
         const Extent e = program_extent(p, pid);
-        if (!wait_bounded(smem_addr(&tempty[acc]), acc_phase ^ 1u, abort_flag, kSiteMma)) break;
+        if (!warp_wait(smem_addr(&tempty[acc]), acc_phase ^ 1u, abort_flag, kSiteMma, lane, prof_te)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         if (e.nkb == 0) {
-          mbar_arrive(smem_addr(&tfull[acc]));
+          if (elect_one()) {
+            mbar_arrive(smem_addr(&tfull[acc]));
+            if constexpr (G == 2) mbar_arrive_cluster(map_to_cta(smem_addr(&tfull[acc]), 1));
+          }
+          __syncwarp();
         } else {
           for (int kb = 0; kb < e.nkb; ++kb) {
-            if (!wait_bounded(smem_addr(&full[stage]), phase, abort_flag, kSiteMma)) {
+            if (!warp_wait(smem_addr(&full[stage]), phase, abort_flag, kSiteMma, lane, prof_full)) {
               ok = false;
               break;
             }
             tc_fence_after();
             const int kvalid = min(kBK, e.k_end - (e.k_begin + kb * kBK));
-            const int nk16 = (kvalid + 15) / 16;
             const uint32_t a0 = smem_addr(sA + (size_t)stage * kABytes);
-            const uint32_t b0 = smem_addr(sB + (size_t)stage * C::kBBytes);
-            for (int kk = 0; kk < nk16; ++kk) {
-              // A: K-major rows of 128 B; 8-row groups 1024 B apart; a K step
-              // of 16 elements is 32 B inside the swizzle atom.
-              const uint64_t da = smem_desc_sw128(a0 + kk * 32, 16, 1024);
-              // B: N-major; 64-column boxes kBBoxBytes apart (LBO), 8-row K
-              // groups 1024 B apart (SBO); 16 K rows are 2048 B.
-              const uint64_t db = smem_desc_sw128(b0 + kk * 2048, kBBoxBytes, 1024);
-              umma_f16(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            const uint32_t b0 = smem_addr(sB + (size_t)stage * Cf::kBBytes);
+            // A: K-major rows of 128 B; 8-row groups 1024 B apart; a K step
+            // of 16 elements is 32 B inside the swizzle atom.
+            // B: N-major; 64-column boxes kBBoxBytes apart (LBO), 8-row K
+            // groups 1024 B apart (SBO); 16 K rows are 2048 B.
+            const uint64_t da0 = smem_desc_sw128(a0, 16, 1024);
+            const uint64_t db0 = smem_desc_sw128(b0, kBBoxBytes, 1024);
+            if (elect_one()) {
+              if (kvalid == kBK) {
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk) {
+                  // start-address field is bits [0,14) in 16-byte units
+                  const uint64_t da = da0 + (uint64_t)((kk * 32) >> 4);
+                  const uint64_t db = db0 + (uint64_t)((kk * 2048) >> 4);
+                  if constexpr (G == 2)
+                    umma_f16_pair(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                  else
+                    umma_f16(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                }
+              } else {
+                const int nk16 = (kvalid + 15) / 16;
+                for (int kk = 0; kk < nk16; ++kk) {
+                  const uint64_t da = da0 + (uint64_t)((kk * 32) >> 4);
+                  const uint64_t db = db0 + (uint64_t)((kk * 2048) >> 4);
+                  if constexpr (G == 2)
+                    umma_f16_pair(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                  else
+                    umma_f16(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                }
+              }
+              if constexpr (G == 2) umma_commit_pair(smem_addr(&empty[stage]), 0x3);
+              else umma_commit(smem_addr(&empty[stage]));
             }
+            __syncwarp();
             issued_any = true;
-            umma_commit(smem_addr(&empty[stage]));
             if (++stage == S) {
               stage = 0;
               phase ^= 1u;
             }
           }
           if (!ok) break;
-          umma_commit(smem_addr(&tfull[acc]));
+          if (elect_one()) {
+            if constexpr (G == 2) umma_commit_pair(smem_addr(&tfull[acc]), 0x3);
+            else umma_commit(smem_addr(&tfull[acc]));
+          }
+          __syncwarp();
         }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
-      if (!ok && issued_any) {
+      if (lane == 0) {
+        TB_PROF_ADD(1, prof_full);
+        TB_PROF_ADD(2, prof_te);
+      }
+      if (!ok && issued_any && lane == 0) {
         // Aborted with MMAs possibly in flight: wait for them before TMEM goes.
-        umma_commit(smem_addr(drain));
+        if constexpr (G == 2) umma_commit_pair(smem_addr(drain), 0x1);
+        else umma_commit(smem_addr(drain));
         const long long t0 = clock64();
         while (!mbar_try_wait(smem_addr(drain), 0)) {
           if (clock64() - t0 > kWaitBudgetCycles) {
@@ -328,17 +449,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      __syncwarp();
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
+    const int row_in_tile = (int)rank * 128 + q * 32 + lane;
+    const uint32_t tempty_leader0 = G == 2 ? map_to_cta(smem_addr(&tempty[0]), 0) : smem_addr(&tempty[0]);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int32_t pid = blockIdx.x; pid < p.map.total_programs; pid += gridDim.x) {
+    long long prof_tf = 0;
+    for (int32_t pid = first_pid; pid < p.map.total_programs; pid += pid_stride) {
       const Extent e = program_extent(p, pid);
       int ok = 0;
-      if (lane == 0) ok = wait_bounded(smem_addr(&tfull[acc]), acc_phase, abort_flag, kSiteEpilogue);
+      if (lane == 0) ok = wait_prof(smem_addr(&tfull[acc]), acc_phase, abort_flag, kSiteEpilogue, 3, prof_tf);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
@@ -400,16 +524,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&tempty[acc]));
+      if (lane == 0) {
+        if constexpr (G == 2) mbar_arrive_cluster(tempty_leader0 + acc * 8);
+        else mbar_arrive(smem_addr(&tempty[acc]));
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (lane == 0 && q == 0) TB_PROF_ADD(3, prof_tf);
   }
 
   __syncthreads();
+#ifdef TB_WAIT_PROFILE
+  if (threadIdx.x == 0) TB_PROF_ADD(4, clock64() - kernel_t0);
+#endif
+  if constexpr (G == 2) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    tmem_dealloc_g<G>(tmem_base, Cf::kTmemCols);
   }
 }
 
@@ -494,23 +626,36 @@ tbStatus encode_f16_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t
 }
 
 constexpr int kMaxDevices = 64;
-std::atomic<bool> g_attr_set[3][2][kMaxDevices];
+constexpr int kNumTiles = 5;
+std::atomic<bool> g_attr_set[kNumTiles][2][kMaxDevices];
 
-template <int BN, typename OutT>
+template <int BN, int G, typename OutT>
 tbStatus launch_gemm(const tb_matmul_plan* plan, const CUtensorMap& ta, const CUtensorMap& tb_,
                      const KParams& kp, cudaStream_t stream, int kt, int ot) {
-  auto kern = tb_gemm_sm100_kernel<BN, OutT>;
+  auto kern = tb_gemm_sm100_kernel<BN, G, OutT>;
+  constexpr size_t smem = Cfg<BN, G>::kSmem;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices || !g_attr_set[kt][ot][dev].load()) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)Cfg<BN>::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess)
       return tb_fail(TB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     if (dev >= 0 && dev < kMaxDevices) g_attr_set[kt][ot][dev].store(true);
   }
-  kern<<<(unsigned)plan->grid, kThreads, Cfg<BN>::kSmem, stream>>>(ta, tb_, kp);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)plan->grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = G;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb_, kp);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess)
     return tb_fail(TB_ERR_CUDA, std::string("tb_gemm_sm100 launch: ") + cudaGetErrorString(e));
   return TB_OK;
@@ -520,9 +665,11 @@ template <typename OutT>
 tbStatus dispatch_tile(const tb_matmul_plan* plan, const CUtensorMap& ta, const CUtensorMap& tb_,
                        const KParams& kp, cudaStream_t stream, int ot) {
   switch (plan->kernel_tile) {
-    case kTile128x64: return launch_gemm<64, OutT>(plan, ta, tb_, kp, stream, 0, ot);
-    case kTile128x128: return launch_gemm<128, OutT>(plan, ta, tb_, kp, stream, 1, ot);
-    case kTile128x256: return launch_gemm<256, OutT>(plan, ta, tb_, kp, stream, 2, ot);
+    case kTile128x64: return launch_gemm<64, 1, OutT>(plan, ta, tb_, kp, stream, 0, ot);
+    case kTile128x128: return launch_gemm<128, 1, OutT>(plan, ta, tb_, kp, stream, 1, ot);
+    case kTile128x256: return launch_gemm<256, 1, OutT>(plan, ta, tb_, kp, stream, 2, ot);
+    case kTile256x128: return launch_gemm<128, 2, OutT>(plan, ta, tb_, kp, stream, 3, ot);
+    case kTile256x256: return launch_gemm<256, 2, OutT>(plan, ta, tb_, kp, stream, 4, ot);
   }
   return tb_fail(TB_ERR_UNSUPPORTED, "unknown kernel tile");
 }
@@ -533,18 +680,22 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 size_t tb_kernel_smem_bytes(int32_t kernel_tile, int32_t /*stages*/) {
   switch (kernel_tile) {
-    case kTile128x64: return Cfg<64>::kSmem;
-    case kTile128x128: return Cfg<128>::kSmem;
-    case kTile128x256: return Cfg<256>::kSmem;
+    case kTile128x64: return Cfg<64, 1>::kSmem;
+    case kTile128x128: return Cfg<128, 1>::kSmem;
+    case kTile128x256: return Cfg<256, 1>::kSmem;
+    case kTile256x128: return Cfg<128, 2>::kSmem;
+    case kTile256x256: return Cfg<256, 2>::kSmem;
   }
   return 0;
 }
 
 int32_t tb_kernel_max_stages(int32_t kernel_tile) {
   switch (kernel_tile) {
-    case kTile128x64: return Cfg<64>::kStages;
-    case kTile128x128: return Cfg<128>::kStages;
-    case kTile128x256: return Cfg<256>::kStages;
+    case kTile128x64: return Cfg<64, 1>::kStages;
+    case kTile128x128: return Cfg<128, 1>::kStages;
+    case kTile128x256: return Cfg<256, 1>::kStages;
+    case kTile256x128: return Cfg<128, 2>::kStages;
+    case kTile256x256: return Cfg<256, 2>::kStages;
   }
   return 0;
 }
@@ -627,6 +778,17 @@ tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda, const
   }
   return TB_OK;
 }
+
+#ifdef TB_WAIT_PROFILE
+extern "C" int tb_debug_wait_profile(unsigned long long* out8, int reset) {
+  if (cudaMemcpyFromSymbol(out8, g_tb_prof, sizeof(unsigned long long) * 8) != cudaSuccess) return 1;
+  if (reset) {
+    unsigned long long z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    cudaMemcpyToSymbol(g_tb_prof, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
 
 extern "C" tbStatus tb_device_status(void* stream, uint32_t* raw) {
   cudaError_t e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));

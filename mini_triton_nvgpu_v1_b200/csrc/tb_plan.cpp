@@ -269,18 +269,27 @@ extern "C" tbStatus tb_matmul_plan_create(const tb_matmul_desc* desc, int device
   else if (kind == tb::kMapGroupedTile) p.mainline_kind = "grouped_tile";
   else p.mainline_kind = "single_tile";
 
-  // ---- this build's hardware tile (tcgen05 M=128, N ∈ {64,128,256}) ----
-  if (d.block_m > 128)
+  // ---- this build's hardware tile: tcgen05 M=128 on one CTA, or M=256 on a
+  //      CTA pair (cta_group::2); N ∈ {64, 128, 256} ----
+  if (d.block_m > 256)
     return tb_fail(TB_ERR_UNSUPPORTED,
-                   "block_m > 128 is not supported by the sm_100a kernels of "
-                   "this build (one tcgen05 M=128 accumulator per program)");
+                   "block_m > 256 is not supported by the sm_100a kernels of this "
+                   "build (one tcgen05 accumulator of at most 256 rows per program)");
   if (d.block_n > 256)
     return tb_fail(TB_ERR_UNSUPPORTED,
                    "block_n > 256 is not supported (tcgen05 N <= 256)");
-  p.cta_m = 128;
-  if (d.block_n <= 64) { p.kernel_tile = kTile128x64; p.cta_n = 64; }
-  else if (d.block_n <= 128) { p.kernel_tile = kTile128x128; p.cta_n = 128; }
-  else { p.kernel_tile = kTile128x256; p.cta_n = 256; }
+  if (d.block_m <= 128) {
+    p.cta_m = 128;
+    p.ctas_per_tile = 1;
+    if (d.block_n <= 64) { p.kernel_tile = kTile128x64; p.cta_n = 64; }
+    else if (d.block_n <= 128) { p.kernel_tile = kTile128x128; p.cta_n = 128; }
+    else { p.kernel_tile = kTile128x256; p.cta_n = 256; }
+  } else {
+    p.cta_m = 256;
+    p.ctas_per_tile = 2;
+    if (d.block_n <= 128) { p.kernel_tile = kTile256x128; p.cta_n = 128; }
+    else { p.kernel_tile = kTile256x256; p.cta_n = 256; }
+  }
   // The ring is as deep as shared memory allows and never shallower than
   // tb.requested-stages.
   p.stages = std::max<int32_t>((int32_t)d.num_stages, tb_kernel_max_stages(p.kernel_tile));
@@ -303,8 +312,10 @@ extern "C" tbStatus tb_matmul_plan_create(const tb_matmul_desc* desc, int device
     p.epilogue = kEpiStore;
     p.workspace_bytes = 0;
   }
+  // Resident program slots: one per SM, or one per SM pair for CTA pairs.
   const int64_t want = d.persistent ? p.resident_programs : total;
-  p.grid = std::max<int64_t>(1, std::min<int64_t>(want, num_sms));
+  const int64_t slots = std::max<int64_t>(1, num_sms / p.ctas_per_tile);
+  p.grid = p.ctas_per_tile * std::max<int64_t>(1, std::min<int64_t>(want, slots));
 
   tb_matmul_plan* heap = new (std::nothrow) tb_matmul_plan(p);
   if (!heap) return tb_fail(TB_ERR_INVALID_ARGUMENT, "out of host memory");
@@ -340,7 +351,8 @@ extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* bu
   if (!plan) return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan must not be NULL");
   const tb_matmul_desc& d = plan->desc;
   const char* kernel_names[] = {"tb_gemm_sm100_128x64", "tb_gemm_sm100_128x128",
-                                "tb_gemm_sm100_128x256"};
+                                "tb_gemm_sm100_128x256", "tb_gemm_sm100_pair_256x128",
+                                "tb_gemm_sm100_pair_256x256"};
   const char* epi_names[] = {"store", "workspace_partial", "atomic_add"};
   std::ostringstream o;
   o << "{";
@@ -374,6 +386,7 @@ extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* bu
   o << "\"num_sms\": " << plan->num_sms << ", ";
   o << "\"kernel\": \"" << kernel_names[plan->kernel_tile] << "\", ";
   o << "\"cta_tile\": [" << plan->cta_m << ", " << plan->cta_n << ", 64], ";
+  o << "\"ctas_per_tile\": " << plan->ctas_per_tile << ", ";
   o << "\"stages\": " << plan->stages << ", ";
   o << "\"smem_bytes\": " << plan->smem_bytes << ", ";
   o << "\"tmem_cols\": " << plan->tmem_cols << ", ";

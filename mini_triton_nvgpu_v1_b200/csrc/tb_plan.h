@@ -15,6 +15,8 @@ enum TbKernelTile : int32_t {
   kTile128x64 = 0,
   kTile128x128 = 1,
   kTile128x256 = 2,
+  kTile256x128 = 3,  // CTA pair (cta_group::2)
+  kTile256x256 = 4,  // CTA pair (cta_group::2)
 };
 
 enum TbEpilogue : int32_t {
@@ -45,7 +47,8 @@ struct tb_matmul_plan {
 
   // --- this build's launch facts ---
   int32_t kernel_tile;         // TbKernelTile
-  int32_t cta_m, cta_n;        // hardware tile
+  int32_t cta_m, cta_n;        // hardware tile (cta_m = 256: a CTA pair)
+  int32_t ctas_per_tile;       // 1 or 2
   int32_t stages;              // shared-memory ring depth (64-deep K stages)
   int32_t epilogue;            // TbEpilogue
   int64_t grid;                // CTAs launched

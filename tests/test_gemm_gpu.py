@@ -71,6 +71,20 @@ CASES = [
                                                               split_k=16,
                                                               reduction_mode="split_k_serial"),
      "uniform", 6),
+    ("pair256x256_grouped", (1024, 1024, 1024), dict(block_m=256, block_n=256, block_k=64, group_m=8),
+     "normal", 4),
+    ("pair256x256_ragged", (1000, 1000, 520), dict(block_m=256, block_n=256, block_k=64,
+                                                   exact_tile=False), "uniform", 11),
+    ("pair256x128_ragged_k_tail", (300, 200, 72), dict(block_m=256, block_n=128, block_k=16,
+                                                       exact_tile=False), "uniform", 13),
+    ("pair_block192x200", (800, 640, 256), dict(block_m=192, block_n=200, block_k=64,
+                                                exact_tile=False, group_m=3), "uniform", 14),
+    ("pair_persistent", (1536, 1024, 512), dict(block_m=256, block_n=256, block_k=64,
+                                                persistent=True, num_ctas=64), "uniform", 15),
+    ("pair_splitk_serial", (512, 512, 4096), dict(block_m=256, block_n=256, block_k=64, split_k=8,
+                                                  reduction_mode="split_k_serial"), "uniform", 6),
+    ("pair_splitk_parallel", (512, 512, 2048), dict(block_m=256, block_n=256, block_k=64, split_k=4,
+                                                    reduction_mode="split_k_parallel"), "uniform", 6),
     ("splitk_parallel_512x512x4096_s8", (512, 512, 4096), dict(block_m=128, block_n=128, block_k=64,
                                                                split_k=8,
                                                                reduction_mode="split_k_parallel"),
