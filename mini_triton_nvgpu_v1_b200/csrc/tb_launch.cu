@@ -33,6 +33,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstring>
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -74,10 +75,19 @@ struct Cfg {
   static constexpr int kBnCta = BN / G;                  // B columns per CTA
   static constexpr uint32_t kBBytes = kBnCta * kBK * 2;  // kBnCta/64 boxes
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr int kRawStages = (int)((kSmemLimit - 1024 - 512) / kStageBytes);
-  static constexpr int kStages = kRawStages > 8 ? 8 : kRawStages;
+  // f32 output staging for the TMA-store epilogue: 4 warps × 2 buffers of
+  // [32 rows × 32 f32] (128-byte swizzled rows).
+  static constexpr uint32_t kEpiBufBytes = 32 * 32 * 4;
+  static constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBufBytes;
+  static constexpr int kRawStages = (int)((kSmemLimit - 1024 - 512 - kEpiBytes) / kStageBytes);
+#ifdef TB_DEBUG_MAX_STAGES
+  static constexpr int kCap = TB_DEBUG_MAX_STAGES;  // debug builds: ring-depth experiments
+#else
+  static constexpr int kCap = 8;
+#endif
+  static constexpr int kStages = kRawStages > kCap ? kCap : kRawStages;
   static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators of BN f32 columns
-  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 512;
+  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + kEpiBytes + 512;
   static_assert(kBnCta % 64 == 0, "B columns per CTA must be whole 64-column boxes");
   static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512, "TMEM columns");
 };
@@ -90,6 +100,7 @@ struct KParams {
   int32_t beta;
   int32_t vec_c;     // C rows allow 16-byte vector access
   int32_t vec_ws;    // workspace rows allow 16-byte vector access
+  int32_t tma_store; // f32 C written by TMA from swizzled shared staging
   void* C;
   int64_t ldc;
   float* ws;
@@ -223,7 +234,8 @@ struct OutIO<__half> {
 template <int BN, int G, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     tb_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
-                         const __grid_constant__ CUtensorMap tmB, const KParams p) {
+                         const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmC, const KParams p) {
   using Cf = Cfg<BN, G>;
   constexpr int S = Cf::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -231,7 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + (size_t)S * kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)S * Cf::kBBytes);
+  uint8_t* sEpi = sB + (size_t)S * Cf::kBBytes;  // 1024-aligned: stage sizes are multiples of 1 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + Cf::kEpiBytes);
   uint64_t* full = bars;            // leader: A/B of both CTAs landed
   uint64_t* empty = bars + S;       // every CTA: stage consumed by the MMAs
   uint64_t* tfull = bars + 2 * S;   // every CTA: accumulator ready
@@ -264,6 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (p.tma_store) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc_g<G>(smem_addr(tmem_holder), Cf::kTmemCols);
@@ -455,6 +469,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = (int)rank * 128 + q * 32 + lane;
+    uint8_t* epi_buf = sEpi + (size_t)(warp - 2) * 2 * Cf::kEpiBufBytes;
+    uint32_t epi_slot = 0;
     const uint32_t tempty_leader0 = G == 2 ? map_to_cta(smem_addr(&tempty[0]), 0) : smem_addr(&tempty[0]);
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -476,11 +492,56 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = 0.f;
         }
-        if (!row_ok) continue;
         const int ncol = min(32, e.cols - c0);
         const int64_t gcol = (int64_t)e.n0 + c0;
+        if (p.tma_store && p.epilogue == kEpiStore) {
+          // TMA path (exact hardware tile): rows past M take part with
+          // zeros; TMA does not write outside the tensor.
+          if (!row_ok) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          }
+        } else if (!row_ok) {
+          continue;
+        }
         if (p.epilogue == kEpiStore) {
           OutT* dst = reinterpret_cast<OutT*>(p.C) + grow * p.ldc + gcol;
+          if constexpr (sizeof(OutT) == 4) {
+            if (p.tma_store) {
+              // Stage [32 rows × 32 cols] in 128-byte-swizzled shared memory
+              // (row r's 16-byte chunk j lives at chunk j ^ (r % 8): the
+              // warp's float4 writes are bank-conflict free) and let TMA
+              // write it out; stores past M/N are clipped by TMA.
+              if (p.beta && row_ok) {
+                float c[32];
+                if (ncol == 32) {
+                  OutIO<OutT>::load32(dst, c);
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) c[i] = i < ncol ? OutIO<OutT>::load(dst + i) : 0.f;
+                }
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += c[i];
+              }
+              uint8_t* buf = epi_buf + (size_t)(epi_slot & 1) * Cf::kEpiBufBytes;
+              // The store issued two chunks ago must have finished reading buf.
+              if (lane == 0) bulk_wait_group_read<1>();
+              __syncwarp();
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float4* q4 = reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16));
+                *q4 = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              }
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmC, smem_addr(buf), (int32_t)gcol, (int32_t)(grow - lane));
+                bulk_commit_group();
+              }
+              ++epi_slot;
+              continue;
+            }
+          }
           if (ncol == 32 && p.vec_c) {
             if (p.beta) {
               float c[32];
@@ -532,6 +593,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (acc == 0) acc_phase ^= 1u;
     }
     if (lane == 0 && q == 0) TB_PROF_ADD(3, prof_tf);
+    // Outstanding TMA stores must finish before the CTA (and its shared
+    // memory) goes away.
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 
   __syncthreads();
@@ -631,7 +696,7 @@ std::atomic<bool> g_attr_set[kNumTiles][2][kMaxDevices];
 
 template <int BN, int G, typename OutT>
 tbStatus launch_gemm(const tb_matmul_plan* plan, const CUtensorMap& ta, const CUtensorMap& tb_,
-                     const KParams& kp, cudaStream_t stream, int kt, int ot) {
+                     const CUtensorMap& tc, const KParams& kp, cudaStream_t stream, int kt, int ot) {
   auto kern = tb_gemm_sm100_kernel<BN, G, OutT>;
   constexpr size_t smem = Cfg<BN, G>::kSmem;
   int dev = 0;
@@ -654,7 +719,7 @@ tbStatus launch_gemm(const tb_matmul_plan* plan, const CUtensorMap& ta, const CU
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb_, kp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb_, tc, kp);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess)
     return tb_fail(TB_ERR_CUDA, std::string("tb_gemm_sm100 launch: ") + cudaGetErrorString(e));
@@ -663,13 +728,13 @@ tbStatus launch_gemm(const tb_matmul_plan* plan, const CUtensorMap& ta, const CU
 
 template <typename OutT>
 tbStatus dispatch_tile(const tb_matmul_plan* plan, const CUtensorMap& ta, const CUtensorMap& tb_,
-                       const KParams& kp, cudaStream_t stream, int ot) {
+                       const CUtensorMap& tc, const KParams& kp, cudaStream_t stream, int ot) {
   switch (plan->kernel_tile) {
-    case kTile128x64: return launch_gemm<64, 1, OutT>(plan, ta, tb_, kp, stream, 0, ot);
-    case kTile128x128: return launch_gemm<128, 1, OutT>(plan, ta, tb_, kp, stream, 1, ot);
-    case kTile128x256: return launch_gemm<256, 1, OutT>(plan, ta, tb_, kp, stream, 2, ot);
-    case kTile256x128: return launch_gemm<128, 2, OutT>(plan, ta, tb_, kp, stream, 3, ot);
-    case kTile256x256: return launch_gemm<256, 2, OutT>(plan, ta, tb_, kp, stream, 4, ot);
+    case kTile128x64: return launch_gemm<64, 1, OutT>(plan, ta, tb_, tc, kp, stream, 0, ot);
+    case kTile128x128: return launch_gemm<128, 1, OutT>(plan, ta, tb_, tc, kp, stream, 1, ot);
+    case kTile128x256: return launch_gemm<256, 1, OutT>(plan, ta, tb_, tc, kp, stream, 2, ot);
+    case kTile256x128: return launch_gemm<128, 2, OutT>(plan, ta, tb_, tc, kp, stream, 3, ot);
+    case kTile256x256: return launch_gemm<256, 2, OutT>(plan, ta, tb_, tc, kp, stream, 4, ot);
   }
   return tb_fail(TB_ERR_UNSUPPORTED, "unknown kernel tile");
 }
@@ -752,8 +817,27 @@ tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda, const
       return tb_fail(TB_ERR_CUDA, std::string("cudaMemset2DAsync: ") + cudaGetErrorString(e));
   }
 
-  st = d.c_dtype == TB_F16 ? dispatch_tile<__half>(plan, ta, tbm, kp, stream, 1)
-                           : dispatch_tile<float>(plan, ta, tbm, kp, stream, 0);
+  // TMA-store epilogue: f32 C, program tile == hardware tile (so a box never
+  // covers a neighbour program's columns), 16-byte aligned rows.
+  CUtensorMap tcm;
+  memset(&tcm, 0, sizeof(tcm));
+  kp.tma_store = plan->epilogue == kEpiStore && d.c_dtype == TB_F32 && d.block_m == plan->cta_m &&
+                 d.block_n == plan->cta_n && aligned16(Cp) && (ldc % 4 == 0);
+  if (kp.tma_store) {
+    cuuint64_t dims[2] = {(cuuint64_t)d.n, (cuuint64_t)d.m};
+    cuuint64_t strides[1] = {(cuuint64_t)ldc * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Cp, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return tb_fail(TB_ERR_CUDA, "cuTensorMapEncodeTiled(C) failed with CUresult " +
+                                      std::to_string((int)r));
+  }
+
+  st = d.c_dtype == TB_F16 ? dispatch_tile<__half>(plan, ta, tbm, tcm, kp, stream, 1)
+                           : dispatch_tile<float>(plan, ta, tbm, tcm, kp, stream, 0);
   if (st != TB_OK) return st;
 
   if (plan->epilogue == kEpiWorkspace) {
