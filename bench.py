@@ -316,10 +316,13 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (512 MiB per GPU), no flush",
                        "parallelism": f"N-shard x{world}, no collective"},
             "pct_of_peak": round(100.0 * value / world / peak, 2),
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
-                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                         "peak_source": f"{peak_src} bf16 burst",
-                         "frac_of_sustained": round(achieved / peak_sus, 4) if peak_sus else None,
+            "pct_of_peak_note": "of the measured cuBLAS bf16 burst peak per GPU",
+            # The timed region is ~1 s of back-to-back launches under the
+            # 1 kW power cap, so the sustained cuBLAS figure is the denominator.
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_sus,
+                         "unit": "TFLOP/s", "frac": round(achieved / peak_sus, 4),
+                         "peak_source": f"{peak_src} cuBLAS bf16 sustained (MEASURED_PEAKS.json)",
+                         "frac_of_burst": round(achieved / peak, 4),
                          "traffic": traffic_for(kern),
                          "algorithmic_bytes": 2 * (M * K + K * N_PER_GPU) + 8 * M * N_PER_GPU},
             "cpu_baseline": cpu,
