@@ -26,7 +26,24 @@ from . import _capi
 from ._capi import (TB_F16, TB_F32, TB_REDUCTION_SPLIT_K_PARALLEL, TB_REDUCTION_SPLIT_K_SERIAL,
                     TB_REDUCTION_UNSET)
 
-_lib = _capi.load()
+_lib_handle = None
+
+
+def _load_lib():
+    """Loads libtbgemm.so on first use (raises ImportError if it is missing:
+    there is no CPU fallback)."""
+    global _lib_handle
+    if _lib_handle is None:
+        _lib_handle = _capi.load()
+    return _lib_handle
+
+
+class _LazyLib:
+    def __getattr__(self, name):
+        return getattr(_load_lib(), name)
+
+
+_lib = _LazyLib()
 
 __all__ = ["KernelConfig", "MatmulPlan", "TBError", "matmul", "plan_for", "version", "lib"]
 
@@ -36,7 +53,7 @@ _REDUCTION = {None: TB_REDUCTION_UNSET, "": TB_REDUCTION_UNSET,
 
 
 def lib() -> C.CDLL:
-    return _lib
+    return _load_lib()
 
 
 def version() -> str:
@@ -119,7 +136,7 @@ class MatmulPlan:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        lib_ = _lib  # may already be None during interpreter shutdown
+        lib_ = _lib_handle  # may already be None during interpreter shutdown
         if h is not None and h.value and lib_ is not None:
             lib_.tb_matmul_plan_destroy(h)
             self._h = C.c_void_p()
