@@ -136,6 +136,27 @@ tbStatus tb_matmul_run(const tb_matmul_plan* plan, const void* A, int64_t lda,
                        const void* B, int64_t ldb, void* C, int64_t ldc,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of tb_matmul_run. It has no counterpart in the
+ * reference. It is for callers that must not allocate device memory while
+ * they run — an inference engine's plugin that executes inside a memory plan
+ * fixed ahead of time, a process whose device memory is reserved up front, or
+ * code on a path where an allocator call (and the synchronisation it can
+ * bring) is not allowed. Those callers still pass A, B and C.
+ *
+ * Scratch (the split_k_serial partial planes) comes from one fixed 16 MiB
+ * (16777216-byte) array inside the library, which every GPU that loads the
+ * library holds until the process exits; a plan needing more returns
+ * TB_ERR_WORKSPACE without launching. No cudaMalloc/cudaFree or other
+ * allocating routine is called. The first call on a device looks the array's
+ * device address up (once per device); make that first call before any
+ * stream capture. All calls share the one array: two calls whose kernels
+ * overlap on the GPU (different streams, or different host threads) race on
+ * it. Nothing in it needs to start at zero — each call writes every partial
+ * before it reads it. */
+tbStatus tb_matmul_run_no_alloc(const tb_matmul_plan* plan, const void* A,
+                                int64_t lda, const void* B, int64_t ldb,
+                                void* C, int64_t ldc, void* stream);
+
 /* One-call convenience: desc → plan → run → destroy. */
 tbStatus tb_matmul(const tb_matmul_desc* desc, const void* A, int64_t lda,
                    const void* B, int64_t ldb, void* C, int64_t ldc,

@@ -70,6 +70,8 @@ PROTOTYPES = {
     "tb_matmul_program_work": (C.c_int, [C.c_void_p, C.c_int64, C.POINTER(tb_program_work)]),
     "tb_matmul_run": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
                                 C.c_void_p, C.c_int64, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "tb_matmul_run_no_alloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
+                                         C.c_void_p, C.c_int64, C.c_void_p]),
     "tb_matmul": (C.c_int, [C.POINTER(tb_matmul_desc), C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
                             C.c_void_p, C.c_int64, C.c_void_p, C.c_size_t, C.c_void_p]),
     "tb_device_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32)]),

@@ -874,6 +874,64 @@ extern "C" int tb_debug_wait_profile(unsigned long long* out8, int reset) {
 }
 #endif
 
+// ------------------------------------------------ allocation-free entry point
+//
+// Scratch for tb_matmul_run_no_alloc: a fixed device array that lives in the
+// module image, so a call never allocates. 16 MiB holds the split_k_serial
+// partials of, e.g., 512 x 512 with split_k = 16. Every device that loads this
+// library keeps the array until the process exits.
+constexpr size_t kNoAllocScratchBytes = 16u << 20;
+static __device__ __align__(256) unsigned char g_tb_no_alloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_no_alloc_mu;
+void* g_no_alloc_addr[kMaxDevices] = {};
+
+// The host-side name of g_tb_no_alloc_scratch is only a stand-in; its device
+// address is looked up once per device, with that device current.
+tbStatus no_alloc_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return tb_fail(TB_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return tb_fail(TB_ERR_UNSUPPORTED, "device ordinal beyond the library's table");
+  std::lock_guard<std::mutex> lock(g_no_alloc_mu);
+  if (!g_no_alloc_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_tb_no_alloc_scratch);
+    if (e != cudaSuccess || !p)
+      return tb_fail(TB_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") +
+                                      cudaGetErrorString(e));
+    g_no_alloc_addr[dev] = p;
+  }
+  *out = g_no_alloc_addr[dev];
+  return TB_OK;
+}
+}  // namespace
+
+extern "C" tbStatus tb_matmul_run_no_alloc(const tb_matmul_plan* plan, const void* A, int64_t lda,
+                                           const void* B, int64_t ldb, void* C, int64_t ldc,
+                                           void* stream) {
+  tb_clear_error();
+  if (!plan) return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan must not be NULL");
+  const size_t need = plan->workspace_bytes;
+  if (need > kNoAllocScratchBytes)
+    return tb_fail(TB_ERR_WORKSPACE,
+                   "tb_matmul_run_no_alloc: this plan needs " + std::to_string(need) +
+                       " bytes of scratch; the built-in scratch holds at most " +
+                       std::to_string(kNoAllocScratchBytes) +
+                       " bytes (use tb_matmul_run with a caller-owned workspace)");
+  void* scratch = nullptr;
+  if (need > 0) {
+    tbStatus st = no_alloc_scratch_address(&scratch);
+    if (st != TB_OK) return st;
+  }
+  // Every split part writes all of its m x n partial plane before the
+  // reduction reads it, so the scratch needs no clearing between calls.
+  return tb_launch(plan, A, lda, B, ldb, C, ldc, scratch, need > 0 ? kNoAllocScratchBytes : 0, stream);
+}
+
 extern "C" tbStatus tb_device_status(void* stream, uint32_t* raw) {
   cudaError_t e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess)
