@@ -1,0 +1,169 @@
+"""GPU parity at the BASELINE configs' full sizes and against the golden
+vectors of the reference's own statement of tb.matmul.
+
+Full sizes (8192³, 4096³ f16 out, 16384³, 512×512×65536 split-K) are too big
+for the CPU oracle, so they are checked through size-independent properties:
+  * sampled rows: every program's rows are covered by sampling one row per
+    tile row-block and comparing it with the oracle (tolerance 1e-2·sqrt(K/32));
+  * exact scaling: C(A, 2·B) − C_in == 2·(C(A, B) − C_in) bit for bit on
+    beta = 0 results (powers of two scale every product and partial sum
+    exactly in f16/f32 barring overflow);
+  * checksum: Σ_rows C = (1ᵀ·A)·B + Σ_rows C_in, computed in float64.
+"""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from conftest import make_inputs
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = sorted((Path(__file__).parent / "golden").glob("golden_*.npz"))
+
+
+def _knobs_for(name, meta):
+    bm, bn, bk = meta["block"]
+    kn = dict(block_m=bm, block_n=bn, block_k=bk, group_m=meta["group_m"],
+              exact_tile=meta["exact_tile"])
+    if name.startswith("golden_splitk"):
+        kn.update(split_k=2, reduction_mode="split_k_parallel")
+    if name.startswith("golden_persistent"):
+        kn.update(persistent=True, num_ctas=2)
+    return kn
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[p.stem for p in GOLDEN])
+@pytest.mark.parametrize("variant", ["as_reference", "serial_splitk", "pair_tile"])
+def test_kernel_matches_reference_golden(cuda, path, variant):
+    import torch
+    import mini_triton_nvgpu_v1_b200 as tb
+    import oracle
+    g = np.load(path)
+    meta = json.loads(str(g["meta"]))
+    kn = _knobs_for(path.stem, meta)
+    if variant == "serial_splitk":
+        kn = dict(kn, split_k=max(2, kn.get("split_k", 1)), reduction_mode="split_k_serial",
+                  persistent=False, num_ctas=1)
+    elif variant == "pair_tile":
+        kn = dict(kn, block_m=256, block_n=256, exact_tile=False, split_k=1, reduction_mode=None)
+    tC = torch.from_numpy(g["C_in"].copy()).to(cuda)
+    tb.matmul(torch.from_numpy(g["A"]).to(cuda), torch.from_numpy(g["B"]).to(cuda), tC, **kn)
+    out = tC.cpu().numpy()
+    err = float(np.abs(out - g["C_out"]).max())
+    assert err <= oracle.tolerance(meta["k"]), (kn, err)
+
+
+def _sampled_rows_check(A, B, Cin, out, rows, tol):
+    import oracle
+    ref = oracle.matmul_ref(A[rows], B, Cin[rows])
+    err = float(np.abs(out[rows] - ref).max())
+    assert err <= tol, err
+
+
+def _rows_per_block(m, bm, rng):
+    return np.array(sorted({min(m - 1, t * bm + int(rng.integers(0, bm))) for t in range((m + bm - 1) // bm)}
+                           | {0, m - 1}))
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(shape=(8192, 8192, 8192), knobs=dict(block_m=256, block_n=256, block_k=64, group_m=8),
+         dist="normal", seed=4, out="f32"),
+    dict(shape=(4096, 4096, 4096), knobs=dict(block_m=128, block_n=128, block_k=64, group_m=8),
+         dist="uniform", seed=2, out="f16"),
+    dict(shape=(512, 512, 65536), knobs=dict(block_m=128, block_n=256, block_k=64, split_k=16,
+                                             reduction_mode="split_k_serial"),
+         dist="uniform", seed=6, out="f32"),
+    dict(shape=(512, 512, 65536), knobs=dict(block_m=128, block_n=256, block_k=64, split_k=16,
+                                             reduction_mode="split_k_parallel"),
+         dist="uniform", seed=6, out="f32"),
+    dict(shape=(2048, 2048, 2048), knobs=dict(block_m=256, block_n=256, block_k=64, persistent=True,
+                                              num_ctas=148), dist="uniform", seed=7, out="f16"),
+], ids=["grouped_8192", "ragged_scaleup_4096_f16", "splitk_serial_skinny", "splitk_parallel_skinny",
+        "persistent_2048_f16"])
+def test_fullsize_sampled_rows_and_checksum(cuda, cfg):
+    import torch
+    import mini_triton_nvgpu_v1_b200 as tb
+    import oracle
+    m, n, k = cfg["shape"]
+    rng = np.random.default_rng(cfg["seed"])
+    A, B, Cin = make_inputs(m, n, k, cfg["seed"], cfg["dist"])
+    tA, tB = torch.from_numpy(A).to(cuda), torch.from_numpy(B).to(cuda)
+    tol = oracle.tolerance(k)
+    if cfg["out"] == "f16":
+        Cin = Cin.astype(np.float16).astype(np.float32)
+    tC = torch.from_numpy(Cin).to(cuda)
+    tb.matmul(tA, tB, tC, **cfg["knobs"])
+    out = tC.cpu().numpy()
+    rows = _rows_per_block(m, cfg["knobs"]["block_m"], rng)
+    _sampled_rows_check(A, B, Cin, out, rows, tol)
+    # checksum over all rows, in float64 on the GPU
+    colsum_ref = (torch.from_numpy(A).to(cuda).double().sum(0) @ tB.double()) + \
+        torch.from_numpy(Cin).to(cuda).double().sum(0)
+    colsum = tC.double().sum(0)
+    assert float((colsum - colsum_ref).abs().max()) <= tol * m ** 0.5 * 4
+    if cfg["out"] == "f16":
+        # f16 output = the f32 result of the same launch rounded to f16
+        tC16 = torch.from_numpy(Cin.astype(np.float16)).to(cuda)
+        tb.matmul(tA, tB, tC16, **cfg["knobs"])
+        want = torch.from_numpy(out).to(cuda).half().float()
+        diff = (tC16.float() - want).abs()
+        ulp = torch.from_numpy(np.spacing(want.cpu().numpy().astype(np.float16)).astype(np.float32)).to(cuda).abs()
+        assert bool((diff <= ulp + 1e-6).all())
+
+
+def test_fullsize_16384_sampled(cuda):
+    """16384³ pair-tile GEMM (the largest config of the persistent sweep)."""
+    import torch
+    import mini_triton_nvgpu_v1_b200 as tb
+    m = n = k = 16384
+    g = torch.Generator(device=cuda).manual_seed(8)
+    tA = (torch.rand(m, k, device=cuda, generator=g) * 2 - 1).half()
+    tB = (torch.rand(k, n, device=cuda, generator=g) * 2 - 1).half()
+    tC = torch.zeros(m, n, device=cuda)
+    tb.matmul(tA, tB, tC, block_m=256, block_n=256, block_k=64, persistent=True, num_ctas=148)
+    import oracle
+    rng = np.random.default_rng(8)
+    rows = _rows_per_block(m, 256, rng)[::4]
+    A_rows = tA[torch.from_numpy(rows).to(cuda)].cpu().numpy()
+    ref = oracle.matmul_ref(A_rows, tB.cpu().numpy())
+    err = float(np.abs(tC[torch.from_numpy(rows).to(cuda)].cpu().numpy() - ref).max())
+    assert err <= oracle.tolerance(k), err
+
+
+@pytest.mark.parametrize("knobs", [dict(block_m=256, block_n=256, block_k=64, group_m=8),
+                                   dict(block_m=128, block_n=256, block_k=64, split_k=8,
+                                        reduction_mode="split_k_serial")])
+def test_power_of_two_scaling_is_exact(cuda, knobs):
+    import torch
+    import mini_triton_nvgpu_v1_b200 as tb
+    m = n = 2048
+    k = 4096
+    g = torch.Generator(device=cuda).manual_seed(11)
+    tA = (torch.rand(m, k, device=cuda, generator=g) * 2 - 1).half()
+    tB = (torch.rand(k, n, device=cuda, generator=g) * 2 - 1).half()
+    c1 = torch.zeros(m, n, device=cuda)
+    c2 = torch.zeros(m, n, device=cuda)
+    tb.matmul(tA, tB, c1, beta=0, **knobs)
+    tb.matmul(tA, tB * 2, c2, beta=0, **knobs)
+    assert torch.equal(c2, c1 * 2)
+
+
+def test_deterministic_serial_split_k(cuda):
+    """split_k_serial reduces partials in a fixed order: repeated runs are
+    bitwise identical."""
+    import torch
+    import mini_triton_nvgpu_v1_b200 as tb
+    g = torch.Generator(device=cuda).manual_seed(12)
+    tA = (torch.rand(512, 16384, device=cuda, generator=g) * 2 - 1).half()
+    tB = (torch.rand(16384, 512, device=cuda, generator=g) * 2 - 1).half()
+    outs = []
+    for _ in range(3):
+        c = torch.zeros(512, 512, device=cuda)
+        tb.matmul(tA, tB, c, block_m=128, block_n=128, block_k=64, split_k=16,
+                  reduction_mode="split_k_serial")
+        outs.append(c)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
