@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "splitk"],
+                    help="gemm8192: the headline 8192^3 N-sharded GEMM; splitk: the skinny "
+                         "512x512x65536 split-K config (K-sharded + reduce-scatter at N>1)")
     return ap.parse_args()
 
 
@@ -339,10 +342,102 @@ def run_ours(args):
     return 0
 
 
+SK_M = SK_N = 512
+SK_K = 65536
+SK_SPLIT = 16
+SK_BLOCK = dict(block_m=128, block_n=256, block_k=64, num_warps=4, num_stages=4)
+
+
+def run_splitk(args):
+    """512 x 512 x 65536 with split_k = 16 (split_k_serial: f32 workspace +
+    ordered reduction). At N > 1 the K dimension is sharded across ranks and
+    the f32 partials are combined by an NCCL reduce-scatter (rank r keeps
+    rows [r·512/N, (r+1)·512/N)). Reported against the HBM roofline."""
+    import torch
+    import torch.distributed as dist
+    import mini_triton_nvgpu_v1_b200 as tb
+    from mini_triton_nvgpu_v1_b200 import parallel as par
+
+    rank, world, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    k0, kr = par.k_shard(SK_K, world, rank, SK_BLOCK["block_k"])
+    g = torch.Generator(device=dev).manual_seed(6)
+    A = (torch.rand(SK_M, SK_K, device=dev, generator=g) * 2 - 1).half()[:, k0:k0 + kr].contiguous()
+    B = (torch.rand(SK_K, SK_N, device=dev, generator=g) * 2 - 1).half()[k0:k0 + kr].contiguous()
+    split_local = max(1, SK_SPLIT // world)
+    cfg = tb.KernelConfig(m=SK_M, n=SK_N, k=kr, split_k=split_local, reduction_mode="split_k_serial",
+                          **SK_BLOCK)
+    plan = tb.MatmulPlan(cfg, local)
+    ws = torch.empty(max(1, plan.workspace_bytes), dtype=torch.uint8, device=dev)
+    r0, mr = par.row_shard(SK_M, world, rank)
+    C_rows = torch.zeros(mr, SK_N, device=dev)
+    partial = torch.zeros(SK_M, SK_N, device=dev)
+    recv = torch.empty_like(C_rows)
+
+    def step():
+        if world == 1:
+            plan.run_ptr(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), C_rows.data_ptr(),
+                         SK_N, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+        else:
+            partial.zero_()
+            plan.run_ptr(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), partial.data_ptr(),
+                         SK_N, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+            dist.reduce_scatter_tensor(recv, partial, op=dist.ReduceOp.SUM)
+            C_rows.add_(recv)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    barrier()
+    t = torch.tensor([ev0.elapsed_time(ev1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item()) / args.steps
+    flops = 2.0 * SK_M * SK_N * SK_K
+    bytes_alg = 2.0 * (SK_M * SK_K + SK_K * SK_N) + 8.0 * SK_M * SK_N
+    if rank == 0:
+        hbm = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("hbm_gbs", 6650.0) \
+            if (ROOT / "MEASURED_PEAKS.json").exists() else 6650.0
+        gbs = bytes_alg / world / (ms_step * 1e-3) / 1e9
+        print(json.dumps({
+            "metric": "GEMM TFLOP/s, 512x512x65536 split-K (HBM-roofline config)",
+            "value": round(flops / (ms_step * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "strong", "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"tb.matmul {SK_M}x{SK_N}x{SK_K} split_k={SK_SPLIT} "
+                                   f"({'K-shard x%d + NCCL reduce-scatter' % world if world > 1 else '1 GPU'})",
+                       "split_k_per_rank": split_local, "kernel": plan.info["kernel"]},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4),
+                         "note": "algorithmic bytes per GPU (its A/B K-slice + C_in + C) / step time"},
+            "gpu_launches": args.steps * (2 if world == 1 else 4),
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "splitk":
+        return run_splitk(args)
     return run_ours(args)
 
 

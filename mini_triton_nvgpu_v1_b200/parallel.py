@@ -1,0 +1,91 @@
+"""Multi-GPU partitions of one tb.matmul (one process per GPU).
+
+The reference is single-GPU; these are the two partitions its hot path
+admits on one B200 box:
+
+* N-column sharding (large square shapes): rank r owns columns
+  [n0_r, n0_r + n_r) of B and C, A is replicated, and each rank runs the
+  single-GPU op on its slice — no communication.
+* K sharding (skinny / split-K shapes): rank r owns A[:, K_r] and B[K_r, :],
+  computes the partial P_r = A_r·B_r in f32, and a reduce-scatter (sum) over
+  the ranks leaves rank r with rows [m0_r, m0_r + m_r) of Σ_r P_r, to which it
+  adds its rows of C_in. This is the split-K reduction of the reference
+  (ReductionPlan.cpp:137-192) with the split parts on different GPUs.
+
+`local_matmul` lets the host logic run with any local GEMM (the CPU oracle
+in gloo tests); the default is this package's sm_100a kernel.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+
+def balanced_shard(total: int, world: int, rank: int, align: int = 1) -> tuple[int, int]:
+    """[start, start + size) of `rank`'s share of `total` items, in units of
+    `align` (the last rank takes the ragged remainder)."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    if align <= 0:
+        raise ValueError("align must be positive")
+    units = (total + align - 1) // align
+    base, extra = divmod(units, world)
+    u0 = rank * base + min(rank, extra)
+    u1 = u0 + base + (1 if rank < extra else 0)
+    start = min(total, u0 * align)
+    end = min(total, u1 * align)
+    return start, end - start
+
+
+def column_shard(n: int, world: int, rank: int, block_n: int) -> tuple[int, int]:
+    """Columns of B/C owned by `rank` under N-sharding, whole program tiles
+    (block_n) per rank so every rank runs the same tile shape."""
+    return balanced_shard(n, world, rank, align=block_n)
+
+
+def k_shard(k: int, world: int, rank: int, block_k: int) -> tuple[int, int]:
+    """K range of `rank` under K-sharding, whole block_k tiles, which also
+    keeps every A column offset a multiple of 16 elements (TMA alignment)."""
+    return balanced_shard(k, world, rank, align=block_k)
+
+
+def row_shard(m: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows of C that `rank` receives from the reduce-scatter (equal slices;
+    m must divide by world)."""
+    if m % world:
+        raise ValueError("K-sharded tb.matmul needs m divisible by the world size")
+    return rank * (m // world), m // world
+
+
+def _default_local_matmul():
+    from . import matmul
+    return matmul
+
+
+def matmul_nshard(A, B_local, C_local, local_matmul: Optional[Callable] = None, **knobs):
+    """N-sharded tb.matmul: C_local ← C_local + A·B_local (no collective)."""
+    f = local_matmul or _default_local_matmul()
+    return f(A, B_local, C_local, **knobs)
+
+
+def matmul_kshard(A_local, B_local, C_rows, group=None, local_matmul: Optional[Callable] = None,
+                  partial=None, **knobs):
+    """K-sharded tb.matmul with a reduce-scatter.
+
+    A_local: [m, k_r] (this rank's K columns of A), B_local: [k_r, n],
+    C_rows: [m / world, n] f32 — this rank's rows of C, updated in place to
+    C_in + Σ_r A_r·B_r. `partial` ([m, n] f32 scratch) is allocated when
+    omitted. Returns C_rows."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    m, n = A_local.shape[0], B_local.shape[1]
+    if C_rows.shape != (m // world, n) or m % world:
+        raise ValueError("C_rows must be this rank's [m / world, n] slice")
+    if partial is None:
+        partial = torch.empty(m, n, dtype=torch.float32, device=C_rows.device)
+    f = local_matmul or _default_local_matmul()
+    f(A_local, B_local, partial, beta=0, **knobs)
+    recv = torch.empty_like(C_rows)
+    dist.reduce_scatter_tensor(recv, partial, op=dist.ReduceOp.SUM, group=group)
+    C_rows.add_(recv)
+    return C_rows
