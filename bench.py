@@ -345,7 +345,7 @@ def run_ours(args):
 SK_M = SK_N = 512
 SK_K = 65536
 SK_SPLIT = 16
-SK_BLOCK = dict(block_m=128, block_n=256, block_k=64, num_warps=4, num_stages=4)
+SK_BLOCK = dict(block_m=256, block_n=256, block_k=64, num_warps=4, num_stages=4)
 
 
 def run_splitk(args):

@@ -92,6 +92,14 @@ struct Cfg {
   static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512, "TMEM columns");
 };
 
+// How the epilogue hands a finished f32 [32 × 32] chunk to memory.
+enum TmaOut : int32_t {
+  kTmaNone = 0,      // direct per-thread stores
+  kTmaStoreC = 1,    // TMA store into C        (kEpiStore)
+  kTmaReduceC = 2,   // TMA reduce-add into C   (kEpiAtomic)
+  kTmaStoreWs = 3,   // TMA 3-D store into the [S][M][N] workspace (kEpiWorkspace)
+};
+
 struct KParams {
   tb::MappingArgs map;
   int32_t M, N, K;
@@ -100,7 +108,7 @@ struct KParams {
   int32_t beta;
   int32_t vec_c;     // C rows allow 16-byte vector access
   int32_t vec_ws;    // workspace rows allow 16-byte vector access
-  int32_t tma_store; // f32 C written by TMA from swizzled shared staging
+  int32_t tma_out;   // TmaOut: f32 tile output written by TMA from swizzled shared staging
   void* C;
   int64_t ldc;
   float* ws;
@@ -277,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (p.tma_store) tma_prefetch_desc(&tmC);
+    if (p.tma_out != kTmaNone) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc_g<G>(smem_addr(tmem_holder), Cf::kTmemCols);
@@ -494,54 +502,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int ncol = min(32, e.cols - c0);
         const int64_t gcol = (int64_t)e.n0 + c0;
-        if (p.tma_store && p.epilogue == kEpiStore) {
-          // TMA path (exact hardware tile): rows past M take part with
-          // zeros; TMA does not write outside the tensor.
+        if (p.tma_out != kTmaNone) {
+          // TMA path (program tile == hardware tile). Stage [32 rows × 32
+          // cols] in 128-byte-swizzled shared memory (row r's 16-byte chunk j
+          // at chunk j ^ (r % 8): the warp's float4 writes are bank-conflict
+          // free) and let TMA write, reduce-add or store it; rows/columns past
+          // M/N are clipped by TMA, so rows past M carry zeros.
           if (!row_ok) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.f;
           }
-        } else if (!row_ok) {
+          if (p.tma_out == kTmaStoreC && p.beta && row_ok) {
+            const float* src = reinterpret_cast<const float*>(p.C) + grow * p.ldc + gcol;
+            float c[32];
+            if (ncol == 32) {
+              OutIO<float>::load32(src, c);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) c[i] = i < ncol ? OutIO<float>::load(src + i) : 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += c[i];
+          }
+          uint8_t* buf = epi_buf + (size_t)(epi_slot & 1) * Cf::kEpiBufBytes;
+          // The bulk op issued two chunks ago must have finished reading buf.
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4* q4 = reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16));
+            *q4 = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int32_t y = (int32_t)(grow - lane);
+            if (p.tma_out == kTmaStoreC) tma_store_2d(&tmC, smem_addr(buf), (int32_t)gcol, y);
+            else if (p.tma_out == kTmaReduceC) tma_reduce_add_2d(&tmC, smem_addr(buf), (int32_t)gcol, y);
+            else tma_store_3d(&tmC, smem_addr(buf), (int32_t)gcol, y, e.part);
+            bulk_commit_group();
+          }
+          ++epi_slot;
           continue;
         }
+        if (!row_ok) continue;
         if (p.epilogue == kEpiStore) {
           OutT* dst = reinterpret_cast<OutT*>(p.C) + grow * p.ldc + gcol;
-          if constexpr (sizeof(OutT) == 4) {
-            if (p.tma_store) {
-              // Stage [32 rows × 32 cols] in 128-byte-swizzled shared memory
-              // (row r's 16-byte chunk j lives at chunk j ^ (r % 8): the
-              // warp's float4 writes are bank-conflict free) and let TMA
-              // write it out; stores past M/N are clipped by TMA.
-              if (p.beta && row_ok) {
-                float c[32];
-                if (ncol == 32) {
-                  OutIO<OutT>::load32(dst, c);
-                } else {
-#pragma unroll
-                  for (int i = 0; i < 32; ++i) c[i] = i < ncol ? OutIO<OutT>::load(dst + i) : 0.f;
-                }
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] += c[i];
-              }
-              uint8_t* buf = epi_buf + (size_t)(epi_slot & 1) * Cf::kEpiBufBytes;
-              // The store issued two chunks ago must have finished reading buf.
-              if (lane == 0) bulk_wait_group_read<1>();
-              __syncwarp();
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                float4* q4 = reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16));
-                *q4 = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-              }
-              fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0) {
-                tma_store_2d(&tmC, smem_addr(buf), (int32_t)gcol, (int32_t)(grow - lane));
-                bulk_commit_group();
-              }
-              ++epi_slot;
-              continue;
-            }
-          }
           if (ncol == 32 && p.vec_c) {
             if (p.beta) {
               float c[32];
@@ -817,20 +823,35 @@ tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda, const
       return tb_fail(TB_ERR_CUDA, std::string("cudaMemset2DAsync: ") + cudaGetErrorString(e));
   }
 
-  // TMA-store epilogue: f32 C, program tile == hardware tile (so a box never
-  // covers a neighbour program's columns), 16-byte aligned rows.
+  // TMA epilogue: f32 output, program tile == hardware tile (so a box never
+  // covers a neighbour program's rows or columns), 16-byte aligned rows.
   CUtensorMap tcm;
   memset(&tcm, 0, sizeof(tcm));
-  kp.tma_store = plan->epilogue == kEpiStore && d.c_dtype == TB_F32 && d.block_m == plan->cta_m &&
-                 d.block_n == plan->cta_n && aligned16(Cp) && (ldc % 4 == 0);
-  if (kp.tma_store) {
-    cuuint64_t dims[2] = {(cuuint64_t)d.n, (cuuint64_t)d.m};
-    cuuint64_t strides[1] = {(cuuint64_t)ldc * 4};
-    cuuint32_t box[2] = {32, 32};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = g_encode(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Cp, dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  kp.tma_out = kTmaNone;
+  const bool exact_hw_tile = d.block_m == plan->cta_m && d.block_n == plan->cta_n;
+  if (exact_hw_tile && d.c_dtype == TB_F32 && aligned16(Cp) && ldc % 4 == 0) {
+    if (plan->epilogue == kEpiStore) kp.tma_out = kTmaStoreC;
+    if (plan->epilogue == kEpiAtomic) kp.tma_out = kTmaReduceC;
+  }
+  if (exact_hw_tile && plan->epilogue == kEpiWorkspace && aligned16(workspace) && d.n % 4 == 0)
+    kp.tma_out = kTmaStoreWs;
+  if (kp.tma_out != kTmaNone) {
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r;
+    if (kp.tma_out == kTmaStoreWs) {
+      cuuint64_t dims[3] = {(cuuint64_t)d.n, (cuuint64_t)d.m, (cuuint64_t)kp.map.split_k};
+      cuuint64_t strides[2] = {(cuuint64_t)d.n * 4, (cuuint64_t)d.m * (cuuint64_t)d.n * 4};
+      r = g_encode(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, workspace, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+      cuuint64_t dims[2] = {(cuuint64_t)d.n, (cuuint64_t)d.m};
+      cuuint64_t strides[1] = {(cuuint64_t)ldc * 4};
+      r = g_encode(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Cp, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
     if (r != CUDA_SUCCESS)
       return tb_fail(TB_ERR_CUDA, "cuTensorMapEncodeTiled(C) failed with CUresult " +
                                       std::to_string((int)r));

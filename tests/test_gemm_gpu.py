@@ -85,6 +85,12 @@ CASES = [
                                                   reduction_mode="split_k_serial"), "uniform", 6),
     ("pair_splitk_parallel", (512, 512, 2048), dict(block_m=256, block_n=256, block_k=64, split_k=4,
                                                     reduction_mode="split_k_parallel"), "uniform", 6),
+    ("splitk_serial_ragged_tma", (1000, 600, 2048), dict(block_m=128, block_n=256, block_k=64, split_k=5,
+                                                         exact_tile=False,
+                                                         reduction_mode="split_k_serial"), "uniform", 16),
+    ("splitk_parallel_ragged_tma", (1000, 600, 2048), dict(block_m=256, block_n=256, block_k=64,
+                                                           split_k=5, exact_tile=False,
+                                                           reduction_mode="split_k_parallel"), "uniform", 16),
     ("splitk_parallel_512x512x4096_s8", (512, 512, 4096), dict(block_m=128, block_n=128, block_k=64,
                                                                split_k=8,
                                                                reduction_mode="split_k_parallel"),
