@@ -295,6 +295,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if constexpr (G == 2) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // A dependent grid (the split-K reduction) may be scheduled now; it waits
+  // for this grid's completion before reading anything.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -617,22 +620,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // C = beta·C_in + Σ_s ws[s] in a fixed order (split_k_serial): deterministic.
+// HBM bound; every thread keeps up to 8 partial loads in flight. Launched
+// with programmatic dependent launch: the grid may start while the GEMM
+// drains and waits (griddepcontrol.wait) until the GEMM's writes are visible.
 template <typename OutT>
 __global__ void __launch_bounds__(256)
     tb_splitk_reduce_kernel(const float* __restrict__ ws, int32_t S, int32_t M, int32_t N,
                             void* Cv, int64_t ldc, int32_t beta, int32_t vec) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   OutT* C = reinterpret_cast<OutT*>(Cv);
   const int64_t plane = (int64_t)M * N;
-  if (vec) {  // N % 4 == 0 and C rows 16-byte aligned (f32) / 8-byte (f16)
+  if (vec) {  // N % 4 == 0 and C rows aligned for 4-element access
     const int64_t nvec = plane / 4;
+    const float4* w4 = reinterpret_cast<const float4*>(ws);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
          i += (int64_t)gridDim.x * blockDim.x) {
       const int64_t e = i * 4;
       const int64_t r = e / N, c = e % N;
-      float4 acc = reinterpret_cast<const float4*>(ws)[i];
-      for (int s = 1; s < S; ++s) {
-        const float4 t = reinterpret_cast<const float4*>(ws + s * plane)[i];
-        acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
+      float4 acc = __ldcs(w4 + i);
+      for (int s0 = 1; s0 < S; s0 += 8) {
+        float4 t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (s0 + u < S) t[u] = __ldcs(w4 + (int64_t)(s0 + u) * (plane / 4) + i);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (s0 + u < S) {
+            acc.x += t[u].x; acc.y += t[u].y; acc.z += t[u].z; acc.w += t[u].w;
+          }
       }
       OutT* dst = C + r * ldc + c;
       if (beta) {
@@ -871,12 +886,27 @@ tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda, const
     const int64_t cap = (int64_t)plan->num_sms * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
+    cudaLaunchConfig_t rc = {};
+    rc.gridDim = dim3((unsigned)blocks, 1, 1);
+    rc.blockDim = dim3(256, 1, 1);
+    rc.dynamicSmemBytes = 0;
+    rc.stream = stream;
+    cudaLaunchAttribute rattr[1];
+    rattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    rattr[0].val.programmaticStreamSerializationAllowed = 1;
+    rc.attrs = rattr;
+    rc.numAttrs = 1;
+    cudaError_t le;
     if (d.c_dtype == TB_F16)
-      tb_splitk_reduce_kernel<__half><<<(unsigned)blocks, 256, 0, stream>>>(
-          kp.ws, kp.map.split_k, kp.M, kp.N, Cp, ldc, kp.beta, vec);
+      le = cudaLaunchKernelEx(&rc, tb_splitk_reduce_kernel<__half>, (const float*)kp.ws,
+                              (int32_t)kp.map.split_k, kp.M, kp.N, Cp, (int64_t)ldc, kp.beta,
+                              (int32_t)vec);
     else
-      tb_splitk_reduce_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(
-          kp.ws, kp.map.split_k, kp.M, kp.N, Cp, ldc, kp.beta, vec);
+      le = cudaLaunchKernelEx(&rc, tb_splitk_reduce_kernel<float>, (const float*)kp.ws,
+                              (int32_t)kp.map.split_k, kp.M, kp.N, Cp, (int64_t)ldc, kp.beta,
+                              (int32_t)vec);
+    if (le != cudaSuccess)
+      return tb_fail(TB_ERR_CUDA, std::string("tb_splitk_reduce launch: ") + cudaGetErrorString(le));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
       return tb_fail(TB_ERR_CUDA, std::string("tb_splitk_reduce launch: ") + cudaGetErrorString(e));
