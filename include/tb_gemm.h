@@ -157,6 +157,39 @@ tbStatus tb_matmul_run_no_alloc(const tb_matmul_plan* plan, const void* A,
                                 int64_t lda, const void* B, int64_t ldb,
                                 void* C, int64_t ldc, void* stream);
 
+/* ---- K-sharded runs over NVLink peer memory (one process per GPU) ----
+ * The reference is single-GPU; its split-K reduction (ReductionPlan.cpp:137-192,
+ * atomic executor LowerPipelineToNVGPU.cpp:1862-1912) becomes a cross-GPU
+ * reduce-scatter here. Rank r owns rows [r·m/W, (r+1)·m/W) of C and runs the
+ * plan of its K slice (m × n × k_r, f32 C, block_m/block_n equal to the
+ * hardware tile); its GEMM epilogue reduce-adds every partial tile into the
+ * owner's rows through peer-mapped memory, so C_rows ends as
+ * C_rows_in + Σ_r A_r·B_r on every owner. */
+typedef struct tb_peer_handle {
+  unsigned char rows_ipc[64];  /* CUDA IPC handle of the allocation holding C rows */
+  int64_t rows_offset;         /* offset of the C rows inside that allocation */
+  unsigned char flags_ipc[64]; /* CUDA IPC handle of the rank's barrier flags */
+} tb_peer_handle;
+typedef struct tb_peer_comm tb_peer_comm;
+
+/* my_rows: this rank's rows_per_rank × n f32 rows of C (row stride ldc,
+ * cudaMalloc'd memory, e.g. a torch tensor). Fills *my_handle, which every
+ * rank must pass to tb_peer_comm_connect in rank order. */
+tbStatus tb_peer_comm_create(int rank, int world, void* my_rows,
+                             int64_t rows_per_rank, int64_t n, int64_t ldc,
+                             tb_peer_comm** comm, tb_peer_handle* my_handle);
+tbStatus tb_peer_comm_connect(tb_peer_comm* comm, const tb_peer_handle* all);
+/* Stream-ordered barrier across the ranks (bounded device-side wait). */
+tbStatus tb_peer_barrier(tb_peer_comm* comm, void* stream);
+/* barrier → K-sharded GEMM with the reduction into the owners' rows → barrier.
+ * Collective: every rank calls it with the same plan shape. */
+tbStatus tb_matmul_run_kshard_peer(const tb_matmul_plan* plan, tb_peer_comm* comm,
+                                   const void* A, int64_t lda, const void* B,
+                                   int64_t ldb, void* stream);
+/* Synchronises `stream`; TB_ERR_DEVICE_TIMEOUT if a barrier wait gave up. */
+tbStatus tb_peer_comm_status(tb_peer_comm* comm, void* stream, uint32_t* raw);
+tbStatus tb_peer_comm_destroy(tb_peer_comm* comm);
+
 /* One-call convenience: desc → plan → run → destroy. */
 tbStatus tb_matmul(const tb_matmul_desc* desc, const void* A, int64_t lda,
                    const void* B, int64_t ldb, void* C, int64_t ldc,

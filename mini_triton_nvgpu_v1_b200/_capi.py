@@ -60,6 +60,10 @@ class tb_program_work(C.Structure):
     ]
 
 
+class tb_peer_handle(C.Structure):
+    _fields_ = [("rows_ipc", C.c_ubyte * 64), ("rows_offset", C.c_int64), ("flags_ipc", C.c_ubyte * 64)]
+
+
 # Every symbol include/tb_gemm.h declares, with its ctypes prototype.
 PROTOTYPES = {
     "tb_matmul_desc_init": (C.c_int, [C.POINTER(tb_matmul_desc)]),
@@ -74,6 +78,14 @@ PROTOTYPES = {
                                          C.c_void_p, C.c_int64, C.c_void_p]),
     "tb_matmul": (C.c_int, [C.POINTER(tb_matmul_desc), C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
                             C.c_void_p, C.c_int64, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "tb_peer_comm_create": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
+                                      C.POINTER(C.c_void_p), C.POINTER(tb_peer_handle)]),
+    "tb_peer_comm_connect": (C.c_int, [C.c_void_p, C.POINTER(tb_peer_handle)]),
+    "tb_peer_barrier": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "tb_matmul_run_kshard_peer": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p,
+                                            C.c_int64, C.c_void_p]),
+    "tb_peer_comm_status": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_uint32)]),
+    "tb_peer_comm_destroy": (C.c_int, [C.c_void_p]),
     "tb_device_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32)]),
     "tb_last_error": (C.c_char_p, []),
     "tb_version": (C.c_char_p, []),

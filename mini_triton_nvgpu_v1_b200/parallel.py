@@ -89,3 +89,68 @@ def matmul_kshard(A_local, B_local, C_rows, group=None, local_matmul: Optional[C
     dist.reduce_scatter_tensor(recv, partial, op=dist.ReduceOp.SUM, group=group)
     C_rows.add_(recv)
     return C_rows
+
+
+class PeerKShard:
+    """K-sharded tb.matmul whose reduce-scatter is fused into the GEMM (the C
+    ABI's tb_matmul_run_kshard_peer): each rank's epilogue adds its partial
+    tiles straight into the owning rank's rows of C over NVLink.
+
+    C_rows: this rank's [m / world, n] f32 rows of C (CUDA memory, unit minor
+    stride); it is registered once and updated in place by every run. The
+    constructor is collective (it exchanges CUDA IPC handles through
+    `group`, any torch.distributed backend)."""
+
+    def __init__(self, C_rows, group=None):
+        import ctypes as C
+        import torch.distributed as dist
+        from . import _capi, _load_lib, _check
+        self._lib = _load_lib()
+        self._check = _check
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if C_rows.dtype.itemsize != 4 or C_rows.stride(1) != 1 or not C_rows.is_cuda:
+            raise ValueError("C_rows must be an f32 CUDA tensor with unit minor stride")
+        self.C_rows = C_rows
+        self.rows_per_rank, self.n = C_rows.shape
+        self._h = C.c_void_p()
+        mine = _capi.tb_peer_handle()
+        _check(self._lib.tb_peer_comm_create(self.rank, self.world, C.c_void_p(C_rows.data_ptr()),
+                                             self.rows_per_rank, self.n, C_rows.stride(0),
+                                             C.byref(self._h), C.byref(mine)))
+        blobs = [None] * self.world
+        dist.all_gather_object(blobs, bytes(mine), group=group)
+        arr = (_capi.tb_peer_handle * self.world)()
+        for r, b in enumerate(blobs):
+            C.memmove(C.byref(arr[r]), b, C.sizeof(_capi.tb_peer_handle))
+        _check(self._lib.tb_peer_comm_connect(self._h, arr))
+
+    def run(self, plan, A_local, B_local, stream=None):
+        """C_rows ← C_rows + Σ_ranks A_local·B_local restricted to these rows.
+        `plan`: MatmulPlan of the local problem (m × n × k_local)."""
+        import ctypes as C
+        import torch
+        s = stream if stream is not None else torch.cuda.current_stream(A_local.device)
+        self._check(self._lib.tb_matmul_run_kshard_peer(
+            plan._h, self._h, C.c_void_p(A_local.data_ptr()), A_local.stride(0),
+            C.c_void_p(B_local.data_ptr()), B_local.stride(0), C.c_void_p(s.cuda_stream or None)))
+
+    def barrier(self, stream=None):
+        import ctypes as C
+        import torch
+        s = stream if stream is not None else torch.cuda.current_stream(self.C_rows.device)
+        self._check(self._lib.tb_peer_barrier(self._h, C.c_void_p(s.cuda_stream or None)))
+
+    def check(self, stream=None) -> int:
+        """Synchronises; raises TBError(TB_ERR_DEVICE_TIMEOUT) if a barrier gave up."""
+        import ctypes as C
+        import torch
+        s = stream if stream is not None else torch.cuda.current_stream(self.C_rows.device)
+        raw = C.c_uint32(0)
+        self._check(self._lib.tb_peer_comm_status(self._h, C.c_void_p(s.cuda_stream or None), C.byref(raw)))
+        return raw.value
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            self._lib.tb_peer_comm_destroy(self._h)
+            self._h = None
