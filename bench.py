@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "splitk"],
                     help="gemm8192: the headline 8192^3 N-sharded GEMM; splitk: the skinny "
                          "512x512x65536 split-K config (K-sharded + reduce-scatter at N>1)")
+    ap.add_argument("--kshard", default="peer", choices=["peer", "nccl"],
+                    help="splitk at N>1: reduce-scatter fused into the GEMM over NVLink (peer) "
+                         "or an NCCL reduce-scatter after it")
     return ap.parse_args()
 
 
@@ -368,20 +371,24 @@ def run_splitk(args):
     g = torch.Generator(device=dev).manual_seed(6)
     A = (torch.rand(SK_M, SK_K, device=dev, generator=g) * 2 - 1).half()[:, k0:k0 + kr].contiguous()
     B = (torch.rand(SK_K, SK_N, device=dev, generator=g) * 2 - 1).half()[k0:k0 + kr].contiguous()
-    split_local = max(1, SK_SPLIT // world)
-    cfg = tb.KernelConfig(m=SK_M, n=SK_N, k=kr, split_k=split_local, reduction_mode="split_k_serial",
-                          **SK_BLOCK)
+    peer = world > 1 and args.kshard == "peer"
+    split_local = SK_SPLIT if peer else max(1, SK_SPLIT // world)
+    cfg = tb.KernelConfig(m=SK_M, n=SK_N, k=kr, split_k=split_local,
+                          reduction_mode="split_k_parallel" if peer else "split_k_serial", **SK_BLOCK)
     plan = tb.MatmulPlan(cfg, local)
     ws = torch.empty(max(1, plan.workspace_bytes), dtype=torch.uint8, device=dev)
     r0, mr = par.row_shard(SK_M, world, rank)
     C_rows = torch.zeros(mr, SK_N, device=dev)
     partial = torch.zeros(SK_M, SK_N, device=dev)
     recv = torch.empty_like(C_rows)
+    comm = par.PeerKShard(C_rows) if peer else None
 
     def step():
         if world == 1:
             plan.run_ptr(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), C_rows.data_ptr(),
                          SK_N, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+        elif peer:
+            comm.run(plan, A, B)
         else:
             partial.zero_()
             plan.run_ptr(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), partial.data_ptr(),
@@ -419,13 +426,16 @@ def run_splitk(args):
             "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "strong", "dtype": "f16", "data": "synthetic",
             "config": {"workload": f"tb.matmul {SK_M}x{SK_N}x{SK_K} split_k={SK_SPLIT} "
-                                   f"({'K-shard x%d + NCCL reduce-scatter' % world if world > 1 else '1 GPU'})",
+                                   f"({('K-shard x%d, reduce-scatter fused into the GEMM over NVLink' if peer else 'K-shard x%d + NCCL reduce-scatter') % world if world > 1 else '1 GPU'})",
                        "split_k_per_rank": split_local, "kernel": plan.info["kernel"]},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(gbs / hbm, 4),
                          "note": "algorithmic bytes per GPU (its A/B K-slice + C_in + C) / step time"},
-            "gpu_launches": args.steps * (2 if world == 1 else 4),
+            "gpu_launches": args.steps * (2 if world == 1 else 3 if peer else 4),
         }), flush=True)
+    if comm is not None:
+        comm.check()
+        comm.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
