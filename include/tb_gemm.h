@@ -161,9 +161,10 @@ tbStatus tb_matmul_run_no_alloc(const tb_matmul_plan* plan, const void* A,
  * The reference is single-GPU; its split-K reduction (ReductionPlan.cpp:137-192,
  * atomic executor LowerPipelineToNVGPU.cpp:1862-1912) becomes a cross-GPU
  * reduce-scatter here. Rank r owns rows [r·m/W, (r+1)·m/W) of C and runs the
- * plan of its K slice (m × n × k_r, f32 C, block_m/block_n equal to the
- * hardware tile); its GEMM epilogue reduce-adds every partial tile into the
- * owner's rows through peer-mapped memory, so C_rows ends as
+ * plan of its K slice (m × n × k_r, f32 C, split_k_parallel or no split).
+ * The GEMM reduces its split parts into a private staging buffer; one more
+ * kernel adds each staged element once into its owner's rows over NVLink
+ * (peer-mapped memory), between two device-side barriers, so C_rows ends as
  * C_rows_in + Σ_r A_r·B_r on every owner. */
 typedef struct tb_peer_handle {
   unsigned char rows_ipc[64];  /* CUDA IPC handle of the allocation holding C rows */
@@ -181,7 +182,7 @@ tbStatus tb_peer_comm_create(int rank, int world, void* my_rows,
 tbStatus tb_peer_comm_connect(tb_peer_comm* comm, const tb_peer_handle* all);
 /* Stream-ordered barrier across the ranks (bounded device-side wait). */
 tbStatus tb_peer_barrier(tb_peer_comm* comm, void* stream);
-/* barrier → K-sharded GEMM with the reduction into the owners' rows → barrier.
+/* K-sharded GEMM, then barrier → add into the owners' rows → barrier.
  * Collective: every rank calls it with the same plan shape. */
 tbStatus tb_matmul_run_kshard_peer(const tb_matmul_plan* plan, tb_peer_comm* comm,
                                    const void* A, int64_t lda, const void* B,

@@ -98,16 +98,6 @@ enum TmaOut : int32_t {
   kTmaStoreC = 1,    // TMA store into C        (kEpiStore)
   kTmaReduceC = 2,   // TMA reduce-add into C   (kEpiAtomic)
   kTmaStoreWs = 3,   // TMA 3-D store into the [S][M][N] workspace (kEpiWorkspace)
-  kTmaReducePeer = 4,  // TMA reduce-add into the owning rank's C rows (K-sharded, peer memory)
-};
-
-// K-sharded runs: one tensor map per rank over that rank's [rows_per_rank × N]
-// slice of C (peer-mapped memory for the other ranks).
-constexpr int kMaxPeers = 8;
-struct PeerMaps {
-  CUtensorMap maps[kMaxPeers];
-  int32_t world;
-  int32_t rows_per_rank;
 };
 
 struct KParams {
@@ -253,8 +243,7 @@ template <int BN, int G, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     tb_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB,
-                         const __grid_constant__ CUtensorMap tmC, const KParams p,
-                         const __grid_constant__ PeerMaps pm) {
+                         const __grid_constant__ CUtensorMap tmC, const KParams p) {
   using Cf = Cfg<BN, G>;
   constexpr int S = Cf::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -553,14 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int32_t y = (int32_t)(grow - lane);
             if (p.tma_out == kTmaStoreC) tma_store_2d(&tmC, smem_addr(buf), (int32_t)gcol, y);
             else if (p.tma_out == kTmaReduceC) tma_reduce_add_2d(&tmC, smem_addr(buf), (int32_t)gcol, y);
-            else if (p.tma_out == kTmaStoreWs) tma_store_3d(&tmC, smem_addr(buf), (int32_t)gcol, y, e.part);
-            else {
-              // 32-row chunks never straddle two owners (rows_per_rank % 32 == 0)
-              const int32_t owner = y / pm.rows_per_rank;
-              if (owner < pm.world)
-                tma_reduce_add_2d(&pm.maps[owner], smem_addr(buf), (int32_t)gcol,
-                                  y - owner * pm.rows_per_rank);
-            }
+            else tma_store_3d(&tmC, smem_addr(buf), (int32_t)gcol, y, e.part);
             bulk_commit_group();
           }
           ++epi_slot;
@@ -735,8 +717,7 @@ std::atomic<bool> g_attr_set[kNumTiles][2][kMaxDevices];
 
 template <int BN, int G, typename OutT>
 tbStatus launch_gemm(const tb_matmul_plan* plan, const CUtensorMap& ta, const CUtensorMap& tb_,
-                     const CUtensorMap& tc, const KParams& kp, const PeerMaps& pm, cudaStream_t stream,
-                     int kt, int ot) {
+                     const CUtensorMap& tc, const KParams& kp, cudaStream_t stream, int kt, int ot) {
   auto kern = tb_gemm_sm100_kernel<BN, G, OutT>;
   constexpr size_t smem = Cfg<BN, G>::kSmem;
   int dev = 0;
@@ -759,7 +740,7 @@ tbStatus launch_gemm(const tb_matmul_plan* plan, const CUtensorMap& ta, const CU
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb_, tc, kp, pm);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb_, tc, kp);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess)
     return tb_fail(TB_ERR_CUDA, std::string("tb_gemm_sm100 launch: ") + cudaGetErrorString(e));
@@ -768,14 +749,13 @@ tbStatus launch_gemm(const tb_matmul_plan* plan, const CUtensorMap& ta, const CU
 
 template <typename OutT>
 tbStatus dispatch_tile(const tb_matmul_plan* plan, const CUtensorMap& ta, const CUtensorMap& tb_,
-                       const CUtensorMap& tc, const KParams& kp, const PeerMaps& pm, cudaStream_t stream,
-                       int ot) {
+                       const CUtensorMap& tc, const KParams& kp, cudaStream_t stream, int ot) {
   switch (plan->kernel_tile) {
-    case kTile128x64: return launch_gemm<64, 1, OutT>(plan, ta, tb_, tc, kp, pm, stream, 0, ot);
-    case kTile128x128: return launch_gemm<128, 1, OutT>(plan, ta, tb_, tc, kp, pm, stream, 1, ot);
-    case kTile128x256: return launch_gemm<256, 1, OutT>(plan, ta, tb_, tc, kp, pm, stream, 2, ot);
-    case kTile256x128: return launch_gemm<128, 2, OutT>(plan, ta, tb_, tc, kp, pm, stream, 3, ot);
-    case kTile256x256: return launch_gemm<256, 2, OutT>(plan, ta, tb_, tc, kp, pm, stream, 4, ot);
+    case kTile128x64: return launch_gemm<64, 1, OutT>(plan, ta, tb_, tc, kp, stream, 0, ot);
+    case kTile128x128: return launch_gemm<128, 1, OutT>(plan, ta, tb_, tc, kp, stream, 1, ot);
+    case kTile128x256: return launch_gemm<256, 1, OutT>(plan, ta, tb_, tc, kp, stream, 2, ot);
+    case kTile256x128: return launch_gemm<128, 2, OutT>(plan, ta, tb_, tc, kp, stream, 3, ot);
+    case kTile256x256: return launch_gemm<256, 2, OutT>(plan, ta, tb_, tc, kp, stream, 4, ot);
   }
   return tb_fail(TB_ERR_UNSUPPORTED, "unknown kernel tile");
 }
@@ -806,66 +786,9 @@ int32_t tb_kernel_max_stages(int32_t kernel_tile) {
   return 0;
 }
 
-namespace {
-tbStatus launch_impl(const tb_matmul_plan* plan, const void* A, int64_t lda, const void* B,
-                     int64_t ldb, void* Cp, int64_t ldc, void* workspace, size_t workspace_bytes,
-                     void* stream_v, const PeerMaps* peer);
-}  // namespace
-
 tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda, const void* B,
                    int64_t ldb, void* Cp, int64_t ldc, void* workspace, size_t workspace_bytes,
                    void* stream_v) {
-  return launch_impl(plan, A, lda, B, ldb, Cp, ldc, workspace, workspace_bytes, stream_v, nullptr);
-}
-
-// K-sharded run whose epilogue reduce-adds every finished [32 × 32] chunk into
-// the owning rank's C rows (rows_per_rank rows each; peer-mapped pointers in
-// `rows`) with TMA. The plan must have f32 C, no workspace, and a program tile
-// equal to its hardware tile.
-tbStatus tb_launch_peer_reduce(const tb_matmul_plan* plan, const void* A, int64_t lda, const void* B,
-                               int64_t ldb, void* const* rows, int world, int64_t rows_per_rank,
-                               int64_t ldc, void* stream) {
-  const tb_matmul_desc& d = plan->desc;
-  if (world < 1 || world > kMaxPeers)
-    return tb_fail(TB_ERR_INVALID_ARGUMENT, "world must be in [1, 8]");
-  if (d.c_dtype != TB_F32 || plan->epilogue == kEpiWorkspace)
-    return tb_fail(TB_ERR_UNSUPPORTED,
-                   "K-sharded peer reduction needs f32 C and no split_k_serial workspace");
-  if (d.block_m != plan->cta_m || d.block_n != plan->cta_n)
-    return tb_fail(TB_ERR_UNSUPPORTED,
-                   "K-sharded peer reduction needs block_m/block_n equal to the hardware tile");
-  if (rows_per_rank <= 0 || rows_per_rank % 32 != 0 || rows_per_rank * world != d.m)
-    return tb_fail(TB_ERR_INVALID_ARGUMENT,
-                   "K-sharded peer reduction needs m = world * rows_per_rank with rows_per_rank % 32 == 0");
-  if (ldc < d.n || ldc % 4 != 0 || d.n % 4 != 0)
-    return tb_fail(TB_ERR_UNSUPPORTED, "K-sharded peer reduction needs ldc and n multiples of 4");
-  tbStatus st = get_encoder();
-  if (st != TB_OK) return st;
-  PeerMaps pm;
-  memset(&pm, 0, sizeof(pm));
-  pm.world = world;
-  pm.rows_per_rank = (int32_t)rows_per_rank;
-  for (int r = 0; r < world; ++r) {
-    if (!rows[r] || !aligned16(rows[r]))
-      return tb_fail(TB_ERR_INVALID_ARGUMENT, "every rank's C rows must be a 16-byte aligned pointer");
-    cuuint64_t dims[2] = {(cuuint64_t)d.n, (cuuint64_t)rows_per_rank};
-    cuuint64_t strides[1] = {(cuuint64_t)ldc * 4};
-    cuuint32_t box[2] = {32, 32};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult cr = g_encode(&pm.maps[r], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, rows[r], dims, strides, box,
-                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (cr != CUDA_SUCCESS)
-      return tb_fail(TB_ERR_CUDA, "cuTensorMapEncodeTiled(peer C rows) failed with CUresult " +
-                                      std::to_string((int)cr));
-  }
-  return launch_impl(plan, A, lda, B, ldb, rows[0], ldc, nullptr, 0, stream, &pm);
-}
-
-namespace {
-tbStatus launch_impl(const tb_matmul_plan* plan, const void* A, int64_t lda, const void* B,
-                     int64_t ldb, void* Cp, int64_t ldc, void* workspace, size_t workspace_bytes,
-                     void* stream_v, const PeerMaps* peer) {
   const tb_matmul_desc& d = plan->desc;
   if (!A || !B || !Cp) return tb_fail(TB_ERR_INVALID_ARGUMENT, "A, B and C must not be NULL");
   if (lda < d.k || ldb < d.n || ldc < d.n)
@@ -908,7 +831,7 @@ tbStatus launch_impl(const tb_matmul_plan* plan, const void* A, int64_t lda, con
   kp.ldc = ldc;
   kp.ws = reinterpret_cast<float*>(workspace);
 
-  if (plan->epilogue == kEpiAtomic && !d.beta && !peer) {
+  if (plan->epilogue == kEpiAtomic && !d.beta) {
     // C = A·B through atomics: start from zero.
     cudaError_t e = cudaMemset2DAsync(Cp, (size_t)ldc * 4, 0, (size_t)d.n * 4, (size_t)d.m, stream);
     if (e != cudaSuccess)
@@ -927,7 +850,6 @@ tbStatus launch_impl(const tb_matmul_plan* plan, const void* A, int64_t lda, con
   }
   if (exact_hw_tile && plan->epilogue == kEpiWorkspace && aligned16(workspace) && d.n % 4 == 0)
     kp.tma_out = kTmaStoreWs;
-  if (peer) kp.tma_out = kTmaNone;  // the peer maps replace the C map
   if (kp.tma_out != kTmaNone) {
     cuuint32_t box[3] = {32, 32, 1};
     cuuint32_t estr[3] = {1, 1, 1};
@@ -950,12 +872,8 @@ tbStatus launch_impl(const tb_matmul_plan* plan, const void* A, int64_t lda, con
                                       std::to_string((int)r));
   }
 
-  PeerMaps pm_none;
-  memset(&pm_none, 0, sizeof(pm_none));
-  if (peer) kp.tma_out = kTmaReducePeer;
-  const PeerMaps& pmr = peer ? *peer : pm_none;
-  st = d.c_dtype == TB_F16 ? dispatch_tile<__half>(plan, ta, tbm, tcm, kp, pmr, stream, 1)
-                           : dispatch_tile<float>(plan, ta, tbm, tcm, kp, pmr, stream, 0);
+  st = d.c_dtype == TB_F16 ? dispatch_tile<__half>(plan, ta, tbm, tcm, kp, stream, 1)
+                           : dispatch_tile<float>(plan, ta, tbm, tcm, kp, stream, 0);
   if (st != TB_OK) return st;
 
   if (plan->epilogue == kEpiWorkspace) {
@@ -995,7 +913,6 @@ tbStatus launch_impl(const tb_matmul_plan* plan, const void* A, int64_t lda, con
   }
   return TB_OK;
 }
-}  // namespace
 
 #ifdef TB_WAIT_PROFILE
 extern "C" int tb_debug_wait_profile(unsigned long long* out8, int reset) {

@@ -61,9 +61,6 @@ struct tb_matmul_plan {
 tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda,
                    const void* B, int64_t ldb, void* C, int64_t ldc,
                    void* workspace, size_t workspace_bytes, void* stream);
-tbStatus tb_launch_peer_reduce(const tb_matmul_plan* plan, const void* A, int64_t lda,
-                               const void* B, int64_t ldb, void* const* rows, int world,
-                               int64_t rows_per_rank, int64_t ldc, void* stream);
 size_t tb_kernel_smem_bytes(int32_t kernel_tile, int32_t stages);
 int32_t tb_kernel_max_stages(int32_t kernel_tile);
 
