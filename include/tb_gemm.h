@@ -76,7 +76,24 @@ typedef struct tb_matmul_desc {
   int32_t a_dtype, b_dtype;        /* must be TB_F16 */
   int32_t c_dtype;                 /* TB_F32 (reference) or TB_F16 (extension) */
   int32_t beta;                    /* 1: C = C_in + A·B (reference); 0: C = A·B */
+  /* Fused epilogue expressions, applied in this order after the full sum
+   * (the kinds EpiloguePlan.h:61-75 declares — LoadBias/Add, Activation,
+   * Clamp, Convert — which the reference never emits):
+   *   v = A·B + beta·C_in; v += bias[col]; v = act(v); v = clamp(v, lo, hi);
+   *   C = convert(v, c_dtype).
+   * Not available with split_k_parallel (partials are summed in C). */
+  int32_t bias;                    /* 1: runs take a length-n f32 bias (per column) */
+  int32_t activation;              /* tbActivation */
+  int32_t clamp;                   /* 1: clamp to [clamp_lo, clamp_hi] */
+  float clamp_lo, clamp_hi;
 } tb_matmul_desc;
+
+typedef enum tbActivation {
+  TB_ACT_NONE = 0,
+  TB_ACT_RELU = 1,
+  TB_ACT_SILU = 2,      /* v · sigmoid(v) */
+  TB_ACT_GELU_TANH = 3  /* tanh approximation of GELU (Hendrycks & Gimpel) */
+} tbActivation;
 
 typedef struct tb_matmul_plan tb_matmul_plan;
 
@@ -190,6 +207,14 @@ tbStatus tb_matmul_run_kshard_peer(const tb_matmul_plan* plan, tb_peer_comm* com
 /* Synchronises `stream`; TB_ERR_DEVICE_TIMEOUT if a barrier wait gave up. */
 tbStatus tb_peer_comm_status(tb_peer_comm* comm, void* stream, uint32_t* raw);
 tbStatus tb_peer_comm_destroy(tb_peer_comm* comm);
+
+/* tb_matmul_run with the bias of a plan made with desc.bias = 1 (`bias`:
+ * n f32 values, one per column of C; NULL when the plan has no bias). */
+tbStatus tb_matmul_run_epilogue(const tb_matmul_plan* plan, const void* A,
+                                int64_t lda, const void* B, int64_t ldb,
+                                void* C, int64_t ldc, const float* bias,
+                                void* workspace, size_t workspace_bytes,
+                                void* stream);
 
 /* One-call convenience: desc → plan → run → destroy. */
 tbStatus tb_matmul(const tb_matmul_desc* desc, const void* A, int64_t lda,

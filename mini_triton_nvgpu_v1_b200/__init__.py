@@ -96,6 +96,10 @@ class KernelConfig:
     programs_per_tile: int = 0
     c_dtype: str = "f32"
     beta: int = 1
+    # fused epilogue expressions (applied after the full sum, in this order)
+    bias: bool = False                 # runs pass a length-n f32 bias
+    activation: Optional[str] = None   # "relu" | "silu" | "gelu_tanh"
+    clamp: Optional[tuple] = None      # (lo, hi)
 
     def to_desc(self) -> _capi.tb_matmul_desc:
         d = _capi.tb_matmul_desc()
@@ -118,6 +122,11 @@ class KernelConfig:
         d.b_dtype = TB_F16
         d.c_dtype = {"f32": TB_F32, "f16": TB_F16, "bf16": _capi.TB_BF16}.get(self.c_dtype, 99)
         d.beta = int(self.beta)
+        d.bias = 1 if self.bias else 0
+        d.activation = _capi.ACTIVATIONS.get(self.activation, 99)
+        if self.clamp is not None:
+            d.clamp = 1
+            d.clamp_lo, d.clamp_hi = float(self.clamp[0]), float(self.clamp[1])
         return d
 
 
@@ -163,13 +172,19 @@ class MatmulPlan:
         return (w.tile_m, w.tile_n, w.split_part, w.k_tile_begin, w.k_tile_count)
 
     def run_ptr(self, a_ptr: int, lda: int, b_ptr: int, ldb: int, c_ptr: int, ldc: int,
-                ws_ptr: int = 0, ws_bytes: int = 0, stream: int = 0) -> None:
+                ws_ptr: int = 0, ws_bytes: int = 0, stream: int = 0, bias_ptr: int = 0) -> None:
         """Raw-pointer launch (device addresses)."""
+        if bias_ptr or self.cfg.bias:
+            _check(_lib.tb_matmul_run_epilogue(self._h, C.c_void_p(a_ptr), lda, C.c_void_p(b_ptr), ldb,
+                                               C.c_void_p(c_ptr), ldc, C.c_void_p(bias_ptr or None),
+                                               C.c_void_p(ws_ptr or None), ws_bytes,
+                                               C.c_void_p(stream or None)))
+            return
         _check(_lib.tb_matmul_run(self._h, C.c_void_p(a_ptr), lda, C.c_void_p(b_ptr), ldb,
                                   C.c_void_p(c_ptr), ldc, C.c_void_p(ws_ptr or None), ws_bytes,
                                   C.c_void_p(stream or None)))
 
-    def run(self, A, B, Cm, workspace=None, stream=None) -> None:
+    def run(self, A, B, Cm, workspace=None, stream=None, bias=None) -> None:
         """C ← beta·C + A·B in place, on torch CUDA tensors."""
         import torch
         _check_tensors(self.cfg, A, B, Cm)
@@ -180,8 +195,14 @@ class MatmulPlan:
                 workspace = torch.empty(need, dtype=torch.uint8, device=Cm.device)
             ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
         s = stream if stream is not None else torch.cuda.current_stream(Cm.device)
+        bias_ptr = 0
+        if bias is not None:
+            if bias.dtype != torch.float32 or bias.numel() != self.cfg.n or not bias.is_contiguous() \
+                    or not bias.is_cuda:
+                raise TBError(_capi.TB_ERR_INVALID_ARGUMENT, "bias must be a contiguous f32 CUDA vector of n")
+            bias_ptr = bias.data_ptr()
         self.run_ptr(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), Cm.data_ptr(),
-                     Cm.stride(0), ws_ptr, ws_bytes, s.cuda_stream)
+                     Cm.stride(0), ws_ptr, ws_bytes, s.cuda_stream, bias_ptr)
 
 
 def _check_tensors(cfg: KernelConfig, A, B, Cm) -> None:
@@ -222,12 +243,15 @@ def matmul(A, B, Cm, *, block_m: int = 128, block_n: int = 256, block_k: int = 6
            group_m: int = 8, exact_tile: Optional[bool] = None, num_warps: int = 4,
            num_stages: int = 2, split_k: int = 1, reduction_mode: Optional[str] = None,
            persistent: bool = False, num_ctas: int = 1, beta: int = 1, workspace=None,
-           stream=None):
+           stream=None, bias=None, activation: Optional[str] = None, clamp=None):
     """``tb.matmul %A, %B, %C {…}``: C ← C + A·B in place (beta=1, the
     reference semantics) or C ← A·B (beta=0). A [m,k] f16, B [k,n] f16,
     C [m,n] f32 (or f16, this build's extension). Returns C.
 
-    ``exact_tile=None`` picks True when the tile divides the problem."""
+    ``exact_tile=None`` picks True when the tile divides the problem.
+    ``bias`` (f32, length n), ``activation`` ("relu" | "silu" | "gelu_tanh")
+    and ``clamp`` ((lo, hi)) are fused epilogue expressions applied, in that
+    order, to the complete sum before the output conversion."""
     import torch
     m, k = A.shape
     n = B.shape[1]
@@ -237,9 +261,11 @@ def matmul(A, B, Cm, *, block_m: int = 128, block_n: int = 256, block_k: int = 6
                        group_m=group_m, exact_tile=exact_tile, num_warps=num_warps,
                        num_stages=num_stages, split_k=split_k, reduction_mode=reduction_mode,
                        persistent=persistent, num_ctas=num_ctas,
-                       c_dtype="f16" if Cm.dtype == torch.float16 else "f32", beta=beta)
+                       c_dtype="f16" if Cm.dtype == torch.float16 else "f32", beta=beta,
+                       bias=bias is not None, activation=activation,
+                       clamp=tuple(clamp) if clamp is not None else None)
     plan = plan_for(cfg, Cm.device.index if Cm.is_cuda else None)
-    plan.run(A, B, Cm, workspace=workspace, stream=stream)
+    plan.run(A, B, Cm, workspace=workspace, stream=stream, bias=bias)
     return Cm
 
 

@@ -22,6 +22,8 @@ TB_ERR_NCCL = 6
 
 TB_F16, TB_F32, TB_BF16 = 0, 1, 2
 TB_REDUCTION_UNSET, TB_REDUCTION_SPLIT_K_SERIAL, TB_REDUCTION_SPLIT_K_PARALLEL = 0, 1, 2
+TB_ACT_NONE, TB_ACT_RELU, TB_ACT_SILU, TB_ACT_GELU_TANH = 0, 1, 2, 3
+ACTIVATIONS = {None: TB_ACT_NONE, "relu": TB_ACT_RELU, "silu": TB_ACT_SILU, "gelu_tanh": TB_ACT_GELU_TANH}
 
 STATUS_NAMES = {
     TB_OK: "TB_OK",
@@ -50,6 +52,10 @@ class tb_matmul_desc(C.Structure):
         ("a_dtype", C.c_int32), ("b_dtype", C.c_int32),
         ("c_dtype", C.c_int32),
         ("beta", C.c_int32),
+        ("bias", C.c_int32),
+        ("activation", C.c_int32),
+        ("clamp", C.c_int32),
+        ("clamp_lo", C.c_float), ("clamp_hi", C.c_float),
     ]
 
 
@@ -76,6 +82,9 @@ PROTOTYPES = {
                                 C.c_void_p, C.c_int64, C.c_void_p, C.c_size_t, C.c_void_p]),
     "tb_matmul_run_no_alloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
                                          C.c_void_p, C.c_int64, C.c_void_p]),
+    "tb_matmul_run_epilogue": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
+                                         C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_size_t,
+                                         C.c_void_p]),
     "tb_matmul": (C.c_int, [C.POINTER(tb_matmul_desc), C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
                             C.c_void_p, C.c_int64, C.c_void_p, C.c_size_t, C.c_void_p]),
     "tb_peer_comm_create": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,

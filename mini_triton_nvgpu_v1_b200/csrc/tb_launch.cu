@@ -100,6 +100,30 @@ enum TmaOut : int32_t {
   kTmaStoreWs = 3,   // TMA 3-D store into the [S][M][N] workspace (kEpiWorkspace)
 };
 
+// Fused epilogue expressions (EpilogueExprKind: LoadBias/Add, Activation,
+// Clamp), applied to the complete f32 sum before the output conversion.
+struct EpiExprs {
+  const float* bias;  // per column, or null
+  int32_t act;        // tbActivation
+  int32_t clamp;
+  float lo, hi;
+  int32_t any;
+};
+
+__device__ __forceinline__ float apply_exprs(const EpiExprs& x, float v, int64_t col) {
+  if (x.bias) v += __ldg(x.bias + col);
+  if (x.act == TB_ACT_RELU) {
+    v = fmaxf(v, 0.f);
+  } else if (x.act == TB_ACT_SILU) {
+    v = v / (1.f + __expf(-v));
+  } else if (x.act == TB_ACT_GELU_TANH) {
+    // 0.5·v·(1 + tanh(sqrt(2/π)·(v + 0.044715·v³)))
+    v = 0.5f * v * (1.f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
+  }
+  if (x.clamp) v = fminf(fmaxf(v, x.lo), x.hi);
+  return v;
+}
+
 struct KParams {
   tb::MappingArgs map;
   int32_t M, N, K;
@@ -109,6 +133,7 @@ struct KParams {
   int32_t vec_c;     // C rows allow 16-byte vector access
   int32_t vec_ws;    // workspace rows allow 16-byte vector access
   int32_t tma_out;   // TmaOut: f32 tile output written by TMA from swizzled shared staging
+  EpiExprs ex;       // applied in kEpiStore (split_k_serial: in the reduction)
   void* C;
   int64_t ldc;
   float* ws;
@@ -527,6 +552,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] += c[i];
           }
+          if (p.tma_out == kTmaStoreC && p.ex.any) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < ncol) v[i] = apply_exprs(p.ex, v[i], gcol + i);
+          }
           uint8_t* buf = epi_buf + (size_t)(epi_slot & 1) * Cf::kEpiBufBytes;
           // The bulk op issued two chunks ago must have finished reading buf.
           if (lane == 0) bulk_wait_group_read<1>();
@@ -558,6 +588,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] += c[i];
             }
+            if (p.ex.any) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = apply_exprs(p.ex, v[i], gcol + i);
+            }
             OutIO<OutT>::store32(dst, v);
           } else {
 #pragma unroll
@@ -565,6 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (i < ncol) {
                 float r = v[i];
                 if (p.beta) r += OutIO<OutT>::load(dst + i);
+                if (p.ex.any) r = apply_exprs(p.ex, r, gcol + i);
                 OutIO<OutT>::store(dst + i, r);
               }
             }
@@ -626,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <typename OutT>
 __global__ void __launch_bounds__(256)
     tb_splitk_reduce_kernel(const float* __restrict__ ws, int32_t S, int32_t M, int32_t N,
-                            void* Cv, int64_t ldc, int32_t beta, int32_t vec) {
+                            void* Cv, int64_t ldc, int32_t beta, int32_t vec, EpiExprs ex) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   OutT* C = reinterpret_cast<OutT*>(Cv);
   const int64_t plane = (int64_t)M * N;
@@ -656,6 +691,12 @@ __global__ void __launch_bounds__(256)
         acc.z += OutIO<OutT>::load(dst + 2);
         acc.w += OutIO<OutT>::load(dst + 3);
       }
+      if (ex.any) {
+        acc.x = apply_exprs(ex, acc.x, c);
+        acc.y = apply_exprs(ex, acc.y, c + 1);
+        acc.z = apply_exprs(ex, acc.z, c + 2);
+        acc.w = apply_exprs(ex, acc.w, c + 3);
+      }
       OutIO<OutT>::store(dst, acc.x);
       OutIO<OutT>::store(dst + 1, acc.y);
       OutIO<OutT>::store(dst + 2, acc.z);
@@ -669,6 +710,7 @@ __global__ void __launch_bounds__(256)
       for (int s = 1; s < S; ++s) acc += ws[s * plane + e];
       OutT* dst = C + r * ldc + c;
       if (beta) acc += OutIO<OutT>::load(dst);
+      if (ex.any) acc = apply_exprs(ex, acc, c);
       OutIO<OutT>::store(dst, acc);
     }
   }
@@ -789,7 +831,18 @@ int32_t tb_kernel_max_stages(int32_t kernel_tile) {
 tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda, const void* B,
                    int64_t ldb, void* Cp, int64_t ldc, void* workspace, size_t workspace_bytes,
                    void* stream_v) {
+  return tb_launch_ex(plan, A, lda, B, ldb, Cp, ldc, nullptr, workspace, workspace_bytes, stream_v);
+}
+
+tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, const void* B,
+                      int64_t ldb, void* Cp, int64_t ldc, const float* bias, void* workspace,
+                      size_t workspace_bytes, void* stream_v) {
   const tb_matmul_desc& d = plan->desc;
+  if (d.bias && !bias)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "this plan applies a bias: pass it with tb_matmul_run_epilogue");
+  if (!d.bias && bias)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "bias given to a plan made without desc.bias");
   if (!A || !B || !Cp) return tb_fail(TB_ERR_INVALID_ARGUMENT, "A, B and C must not be NULL");
   if (lda < d.k || ldb < d.n || ldc < d.n)
     return tb_fail(TB_ERR_INVALID_ARGUMENT, "leading dimensions must be >= the row length");
@@ -824,6 +877,12 @@ tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda, const
   kp.block_k = (int32_t)d.block_k;
   kp.epilogue = plan->epilogue;
   kp.beta = d.beta ? 1 : 0;
+  kp.ex.bias = d.bias ? bias : nullptr;
+  kp.ex.act = d.activation;
+  kp.ex.clamp = d.clamp;
+  kp.ex.lo = d.clamp_lo;
+  kp.ex.hi = d.clamp_hi;
+  kp.ex.any = (d.bias || d.activation != TB_ACT_NONE || d.clamp) ? 1 : 0;
   kp.vec_c = aligned16(Cp) && ((ldc * (int64_t)out_bytes) % 16 == 0) &&
              ((d.block_n * (int64_t)out_bytes) % 16 == 0);
   kp.vec_ws = (d.n % 4 == 0) && (d.block_n % 4 == 0) && aligned16(workspace);
@@ -900,11 +959,11 @@ tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda, const
     if (d.c_dtype == TB_F16)
       le = cudaLaunchKernelEx(&rc, tb_splitk_reduce_kernel<__half>, (const float*)kp.ws,
                               (int32_t)kp.map.split_k, kp.M, kp.N, Cp, (int64_t)ldc, kp.beta,
-                              (int32_t)vec);
+                              (int32_t)vec, kp.ex);
     else
       le = cudaLaunchKernelEx(&rc, tb_splitk_reduce_kernel<float>, (const float*)kp.ws,
                               (int32_t)kp.map.split_k, kp.M, kp.N, Cp, (int64_t)ldc, kp.beta,
-                              (int32_t)vec);
+                              (int32_t)vec, kp.ex);
     if (le != cudaSuccess)
       return tb_fail(TB_ERR_CUDA, std::string("tb_splitk_reduce launch: ") + cudaGetErrorString(le));
     cudaError_t e = cudaGetLastError();

@@ -282,6 +282,9 @@ extern "C" tbStatus tb_matmul_run_kshard_peer(const tb_matmul_plan* plan, tb_pee
   if (plan->epilogue == kEpiWorkspace)
     return tb_fail(TB_ERR_UNSUPPORTED, "K-sharded runs reduce split parts with split_k_parallel, "
                                        "not split_k_serial");
+  if (plan->desc.bias || plan->desc.activation != TB_ACT_NONE || plan->desc.clamp)
+    return tb_fail(TB_ERR_UNSUPPORTED, "K-sharded runs sum partials across GPUs: fused epilogue "
+                                       "expressions are not available");
   if (plan->desc.c_dtype != TB_F32 || c->n % 4 != 0 || c->ldc % 4 != 0)
     return tb_fail(TB_ERR_UNSUPPORTED, "K-sharded runs need f32 C and n, ldc multiples of 4");
   // 1. local GEMM of this K slice (touches only this rank's private staging,

@@ -97,6 +97,11 @@ extern "C" tbStatus tb_matmul_desc_init(tb_matmul_desc* d) {
   d->beta = 1;
   d->num_warps = 4;
   d->num_stages = 2;
+  d->bias = 0;
+  d->activation = TB_ACT_NONE;
+  d->clamp = 0;
+  d->clamp_lo = 0.f;
+  d->clamp_hi = 0.f;
   return TB_OK;
 }
 
@@ -296,6 +301,15 @@ extern "C" tbStatus tb_matmul_plan_create(const tb_matmul_desc* desc, int device
   p.smem_bytes = tb_kernel_smem_bytes(p.kernel_tile, p.stages);
   p.tmem_cols = 2 * p.cta_n;  // two accumulators (epilogue/mainloop overlap)
 
+  if (d.activation < TB_ACT_NONE || d.activation > TB_ACT_GELU_TANH)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "unknown epilogue activation");
+  if (d.clamp && !(d.clamp_lo <= d.clamp_hi))
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "epilogue clamp needs clamp_lo <= clamp_hi");
+  const bool exprs = d.bias || d.activation != TB_ACT_NONE || d.clamp;
+  if (exprs && split_k > 1 && d.reduction_mode == TB_REDUCTION_SPLIT_K_PARALLEL)
+    return tb_fail(TB_ERR_UNSUPPORTED,
+                   "fused epilogue expressions need the complete sum: use split_k_serial "
+                   "(split_k_parallel adds partials into C)");
   if (split_k > 1) {
     if (d.reduction_mode == TB_REDUCTION_SPLIT_K_PARALLEL) {
       if (d.c_dtype != TB_F32)
@@ -394,6 +408,19 @@ extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* bu
   o << "\"block_threads\": 192, ";
   o << "\"epilogue\": \"" << epi_names[plan->epilogue] << "\", ";
   o << "\"beta\": " << d.beta << ", ";
+  {
+    // the reference's EpilogueExprKind spelling, in application order
+    const char* acts[] = {"", "activation(relu)", "activation(silu)", "activation(gelu_tanh)"};
+    o << "\"epilogue_exprs\": [";
+    bool first = true;
+    auto item = [&](const std::string& x) { o << (first ? "" : ", ") << "\"" << x << "\""; first = false; };
+    if (d.beta) item("add(c_in)");
+    if (d.bias) { item("load_bias"); item("add"); }
+    if (d.activation) item(acts[d.activation]);
+    if (d.clamp) item("clamp");
+    if (d.c_dtype == TB_F16) item("convert(f16)");
+    o << "], ";
+  }
   o << "\"workspace_bytes\": " << plan->workspace_bytes;
   o << "}";
   const std::string s = o.str();
@@ -410,6 +437,15 @@ extern "C" tbStatus tb_matmul_run(const tb_matmul_plan* plan, const void* A, int
   tb_clear_error();
   if (!plan) return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan must not be NULL");
   return tb_launch(plan, A, lda, B, ldb, C, ldc, workspace, workspace_bytes, stream);
+}
+
+extern "C" tbStatus tb_matmul_run_epilogue(const tb_matmul_plan* plan, const void* A, int64_t lda,
+                                           const void* B, int64_t ldb, void* C, int64_t ldc,
+                                           const float* bias, void* workspace,
+                                           size_t workspace_bytes, void* stream) {
+  tb_clear_error();
+  if (!plan) return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan must not be NULL");
+  return tb_launch_ex(plan, A, lda, B, ldb, C, ldc, bias, workspace, workspace_bytes, stream);
 }
 
 extern "C" tbStatus tb_matmul(const tb_matmul_desc* desc, const void* A, int64_t lda,

@@ -58,6 +58,9 @@ struct tb_matmul_plan {
 };
 
 // Defined in tb_launch.cu.
+tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, const void* B,
+                      int64_t ldb, void* C, int64_t ldc, const float* bias, void* workspace,
+                      size_t workspace_bytes, void* stream);
 tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda,
                    const void* B, int64_t ldb, void* C, int64_t ldc,
                    void* workspace, size_t workspace_bytes, void* stream);

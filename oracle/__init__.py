@@ -65,3 +65,20 @@ def matmul_ref(A: np.ndarray, B: np.ndarray, C_in: np.ndarray | None = None, bet
 def tolerance(k: int) -> float:
     """max|C_gpu − C_ref| bound stated by the north star: 1e-2·sqrt(K/32)."""
     return 1e-2 * float(np.sqrt(k / 32.0))
+
+
+def apply_epilogue(C: np.ndarray, bias=None, activation=None, clamp=None) -> np.ndarray:
+    """The fused epilogue expressions in float64 (the order of the C ABI:
+    bias per column, activation, clamp) applied to an f32 result."""
+    v = C.astype(np.float64)
+    if bias is not None:
+        v = v + np.asarray(bias, np.float64)[None, :]
+    if activation == "relu":
+        v = np.maximum(v, 0.0)
+    elif activation == "silu":
+        v = v / (1.0 + np.exp(-v))
+    elif activation == "gelu_tanh":
+        v = 0.5 * v * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (v + 0.044715 * v ** 3)))
+    if clamp is not None:
+        v = np.clip(v, clamp[0], clamp[1])
+    return v.astype(np.float32)
