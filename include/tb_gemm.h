@@ -86,6 +86,11 @@ typedef struct tb_matmul_desc {
   int32_t activation;              /* tbActivation */
   int32_t clamp;                   /* 1: clamp to [clamp_lo, clamp_hi] */
   float clamp_lo, clamp_hi;
+  /* Operand storage (the reference takes row-major A and B only; these select
+   * the transposed layouts, read directly by TMA/UMMA without a copy):
+   * a_col_major: A is m × k column-major, lda >= m (A^T row-major);
+   * b_col_major: B is k × n column-major, ldb >= k (B^T row-major). */
+  int32_t a_col_major, b_col_major;
 } tb_matmul_desc;
 
 typedef enum tbActivation {

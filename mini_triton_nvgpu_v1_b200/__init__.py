@@ -100,6 +100,9 @@ class KernelConfig:
     bias: bool = False                 # runs pass a length-n f32 bias
     activation: Optional[str] = None   # "relu" | "silu" | "gelu_tanh"
     clamp: Optional[tuple] = None      # (lo, hi)
+    # operand storage: column-major A (m × k, lda >= m) / B (k × n, ldb >= k)
+    a_col_major: bool = False
+    b_col_major: bool = False
 
     def to_desc(self) -> _capi.tb_matmul_desc:
         d = _capi.tb_matmul_desc()
@@ -127,6 +130,8 @@ class KernelConfig:
         if self.clamp is not None:
             d.clamp = 1
             d.clamp_lo, d.clamp_hi = float(self.clamp[0]), float(self.clamp[1])
+        d.a_col_major = 1 if self.a_col_major else 0
+        d.b_col_major = 1 if self.b_col_major else 0
         return d
 
 
@@ -201,7 +206,9 @@ class MatmulPlan:
                     or not bias.is_cuda:
                 raise TBError(_capi.TB_ERR_INVALID_ARGUMENT, "bias must be a contiguous f32 CUDA vector of n")
             bias_ptr = bias.data_ptr()
-        self.run_ptr(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), Cm.data_ptr(),
+        lda = A.stride(1) if self.cfg.a_col_major else A.stride(0)
+        ldb = B.stride(1) if self.cfg.b_col_major else B.stride(0)
+        self.run_ptr(A.data_ptr(), lda, B.data_ptr(), ldb, Cm.data_ptr(),
                      Cm.stride(0), ws_ptr, ws_bytes, s.cuda_stream, bias_ptr)
 
 
@@ -213,13 +220,14 @@ def _check_tensors(cfg: KernelConfig, A, B, Cm) -> None:
     want_c = torch.float32 if cfg.c_dtype == "f32" else torch.float16
     if Cm.dtype != want_c:
         raise TBError(_capi.TB_ERR_INVALID_ARGUMENT, f"C must be {want_c}")
-    for t, name in ((A, "A"), (B, "B"), (Cm, "C")):
+    for t, name, col in ((A, "A", cfg.a_col_major), (B, "B", cfg.b_col_major), (Cm, "C", False)):
         if t.dim() != 2:
             raise TBError(_capi.TB_ERR_INVALID_ARGUMENT, "tb.matmul currently requires rank-2 memrefs")
         if not t.is_cuda:
             raise TBError(_capi.TB_ERR_INVALID_ARGUMENT, f"{name} must be a CUDA tensor")
-        if t.stride(1) != 1:
-            raise TBError(_capi.TB_ERR_UNSUPPORTED, f"{name} must have a unit minor stride")
+        if t.stride(0 if col else 1) != 1:
+            raise TBError(_capi.TB_ERR_UNSUPPORTED,
+                          f"{name} must have a unit stride along its {'rows' if col else 'columns'}")
     if tuple(A.shape) != (cfg.m, cfg.k) or tuple(B.shape) != (cfg.k, cfg.n) or \
             tuple(Cm.shape) != (cfg.m, cfg.n):
         raise TBError(_capi.TB_ERR_INVALID_ARGUMENT, "operand shapes disagree with the plan")
@@ -255,6 +263,9 @@ def matmul(A, B, Cm, *, block_m: int = 128, block_n: int = 256, block_k: int = 6
     import torch
     m, k = A.shape
     n = B.shape[1]
+    # transposed views (unit stride along rows) select the column-major layout
+    a_col = A.stride(1) != 1 and A.stride(0) == 1
+    b_col = B.stride(1) != 1 and B.stride(0) == 1
     if exact_tile is None:
         exact_tile = (m % block_m == 0 and n % block_n == 0 and k % block_k == 0)
     cfg = KernelConfig(m=m, n=n, k=k, block_m=block_m, block_n=block_n, block_k=block_k,
@@ -263,7 +274,8 @@ def matmul(A, B, Cm, *, block_m: int = 128, block_n: int = 256, block_k: int = 6
                        persistent=persistent, num_ctas=num_ctas,
                        c_dtype="f16" if Cm.dtype == torch.float16 else "f32", beta=beta,
                        bias=bias is not None, activation=activation,
-                       clamp=tuple(clamp) if clamp is not None else None)
+                       clamp=tuple(clamp) if clamp is not None else None,
+                       a_col_major=a_col, b_col_major=b_col)
     plan = plan_for(cfg, Cm.device.index if Cm.is_cuda else None)
     plan.run(A, B, Cm, workspace=workspace, stream=stream, bias=bias)
     return Cm

@@ -56,6 +56,7 @@ class tb_matmul_desc(C.Structure):
         ("activation", C.c_int32),
         ("clamp", C.c_int32),
         ("clamp_lo", C.c_float), ("clamp_hi", C.c_float),
+        ("a_col_major", C.c_int32), ("b_col_major", C.c_int32),
     ]
 
 

@@ -134,6 +134,8 @@ struct KParams {
   int32_t vec_ws;    // workspace rows allow 16-byte vector access
   int32_t tma_out;   // TmaOut: f32 tile output written by TMA from swizzled shared staging
   EpiExprs ex;       // applied in kEpiStore (split_k_serial: in the reduction)
+  int32_t a_mn;      // A stored M-major (column-major m × k): MN-major UMMA operand
+  int32_t b_kmaj;    // B stored K-major (column-major k × n): K-major UMMA operand
   void* C;
   int64_t ldc;
   float* ws;
@@ -359,16 +361,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (leader) mbar_expect_tx(fb_local, G * Cf::kStageBytes);
           if constexpr (G == 2) {
             const uint32_t fb = map_to_cta(fb_local, 0);
-            tma_load_2d_pair(dA, &tmA, fb, kx, e.m0 + (int32_t)rank * 128);
+            const int32_t am = e.m0 + (int32_t)rank * 128;
+            const int32_t bn = e.n0 + (int32_t)rank * Cf::kBnCta;
+            if (p.a_mn) {  // two [64 k × 64 m] boxes
+              tma_load_2d_pair(dA, &tmA, fb, am, kx);
+              tma_load_2d_pair(dA + kBBoxBytes, &tmA, fb, am + 64, kx);
+            } else {
+              tma_load_2d_pair(dA, &tmA, fb, kx, am);
+            }
+            if (p.b_kmaj) {  // one [kBnCta n × 64 k] box
+              tma_load_2d_pair(dB, &tmB, fb, kx, bn);
+            } else {
 #pragma unroll
-            for (int j = 0; j < Cf::kBnCta / 64; ++j)
-              tma_load_2d_pair(dB + j * kBBoxBytes, &tmB, fb, e.n0 + (int32_t)rank * Cf::kBnCta + 64 * j,
-                               kx);
+              for (int j = 0; j < Cf::kBnCta / 64; ++j)
+                tma_load_2d_pair(dB + j * kBBoxBytes, &tmB, fb, bn + 64 * j, kx);
+            }
           } else {
-            tma_load_2d(dA, &tmA, fb_local, kx, e.m0);
+            if (p.a_mn) {
+              tma_load_2d(dA, &tmA, fb_local, e.m0, kx);
+              tma_load_2d(dA + kBBoxBytes, &tmA, fb_local, e.m0 + 64, kx);
+            } else {
+              tma_load_2d(dA, &tmA, fb_local, kx, e.m0);
+            }
+            if (p.b_kmaj) {
+              tma_load_2d(dB, &tmB, fb_local, kx, e.n0);
+            } else {
 #pragma unroll
-            for (int j = 0; j < Cf::kBnCta / 64; ++j)
-              tma_load_2d(dB + j * kBBoxBytes, &tmB, fb_local, e.n0 + 64 * j, kx);
+              for (int j = 0; j < Cf::kBnCta / 64; ++j)
+                tma_load_2d(dB + j * kBBoxBytes, &tmB, fb_local, e.n0 + 64 * j, kx);
+            }
           }
         }
         __syncwarp();
@@ -405,7 +426,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Leader CTA only. Whole warp runs the loop; descriptors are computed
     // warp-uniformly and one elected lane issues tcgen05.mma / commit.
     if (leader) {
-      constexpr uint32_t idesc = idesc_f16_f32(kCtaM * G, BN, 0, 1);
+      const uint32_t idesc = idesc_f16_f32(kCtaM * G, BN, p.a_mn ? 1 : 0, p.b_kmaj ? 0 : 1);
+      // Per-operand layout in shared memory (all 128-byte swizzled):
+      //   K-major: rows of 64 k (128 B), 8-row groups 1024 B apart (SBO); a
+      //            K step of 16 elements is 32 B inside the swizzle atom.
+      //   MN-major: [64 k × 64 mn] boxes kBBoxBytes apart (LBO), 8 k-rows
+      //            1024 B apart (SBO); a K step of 16 rows is 2048 B.
+      const uint32_t a_lbo = p.a_mn ? kBBoxBytes : 16u, a_step = p.a_mn ? 2048u : 32u;
+      const uint32_t b_lbo = p.b_kmaj ? 16u : kBBoxBytes, b_step = p.b_kmaj ? 32u : 2048u;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -434,19 +462,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int kvalid = min(kBK, e.k_end - (e.k_begin + kb * kBK));
             const uint32_t a0 = smem_addr(sA + (size_t)stage * kABytes);
             const uint32_t b0 = smem_addr(sB + (size_t)stage * Cf::kBBytes);
-            // A: K-major rows of 128 B; 8-row groups 1024 B apart; a K step
-            // of 16 elements is 32 B inside the swizzle atom.
-            // B: N-major; 64-column boxes kBBoxBytes apart (LBO), 8-row K
-            // groups 1024 B apart (SBO); 16 K rows are 2048 B.
-            const uint64_t da0 = smem_desc_sw128(a0, 16, 1024);
-            const uint64_t db0 = smem_desc_sw128(b0, kBBoxBytes, 1024);
+            const uint64_t da0 = smem_desc_sw128(a0, a_lbo, 1024);
+            const uint64_t db0 = smem_desc_sw128(b0, b_lbo, 1024);
             if (elect_one()) {
               if (kvalid == kBK) {
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; ++kk) {
                   // start-address field is bits [0,14) in 16-byte units
-                  const uint64_t da = da0 + (uint64_t)((kk * 32) >> 4);
-                  const uint64_t db = db0 + (uint64_t)((kk * 2048) >> 4);
+                  const uint64_t da = da0 + (uint64_t)((kk * a_step) >> 4);
+                  const uint64_t db = db0 + (uint64_t)((kk * b_step) >> 4);
                   if constexpr (G == 2)
                     umma_f16_pair(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                   else
@@ -455,8 +479,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               } else {
                 const int nk16 = (kvalid + 15) / 16;
                 for (int kk = 0; kk < nk16; ++kk) {
-                  const uint64_t da = da0 + (uint64_t)((kk * 32) >> 4);
-                  const uint64_t db = db0 + (uint64_t)((kk * 2048) >> 4);
+                  const uint64_t da = da0 + (uint64_t)((kk * a_step) >> 4);
+                  const uint64_t db = db0 + (uint64_t)((kk * b_step) >> 4);
                   if constexpr (G == 2)
                     umma_f16_pair(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                   else
@@ -844,7 +868,10 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   if (!d.bias && bias)
     return tb_fail(TB_ERR_INVALID_ARGUMENT, "bias given to a plan made without desc.bias");
   if (!A || !B || !Cp) return tb_fail(TB_ERR_INVALID_ARGUMENT, "A, B and C must not be NULL");
-  if (lda < d.k || ldb < d.n || ldc < d.n)
+  // Row-major A (m × k, row stride lda) is the reference layout; a_col_major
+  // means A is stored column-major (lda = stride between columns, >= m).
+  // Likewise B (k × n): row-major ldb >= n, column-major ldb >= k.
+  if (lda < (d.a_col_major ? d.m : d.k) || ldb < (d.b_col_major ? d.k : d.n) || ldc < d.n)
     return tb_fail(TB_ERR_INVALID_ARGUMENT, "leading dimensions must be >= the row length");
   if (lda % 8 != 0 || ldb % 8 != 0)
     return tb_fail(TB_ERR_UNSUPPORTED,
@@ -861,9 +888,15 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_v);
 
   CUtensorMap ta, tbm;
-  st = encode_f16_2d(&ta, A, d.m, d.k, lda, kCtaM, "A");
+  if (d.a_col_major)  // storage k × m (m contiguous): [64 k × 64 m] boxes
+    st = encode_f16_2d(&ta, A, d.k, d.m, lda, kBK, "A");
+  else                // storage m × k: [128 m × 64 k] boxes
+    st = encode_f16_2d(&ta, A, d.m, d.k, lda, kCtaM, "A");
   if (st != TB_OK) return st;
-  st = encode_f16_2d(&tbm, B, d.k, d.n, ldb, kBK, "B");
+  if (d.b_col_major)  // storage n × k (k contiguous): [BN/G n × 64 k] boxes
+    st = encode_f16_2d(&tbm, B, d.n, d.k, ldb, (uint32_t)(plan->cta_n / plan->ctas_per_tile), "B");
+  else                // storage k × n: [64 k × 64 n] boxes
+    st = encode_f16_2d(&tbm, B, d.k, d.n, ldb, kBK, "B");
   if (st != TB_OK) return st;
 
   const size_t out_bytes = d.c_dtype == TB_F16 ? 2 : 4;
@@ -877,6 +910,8 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   kp.block_k = (int32_t)d.block_k;
   kp.epilogue = plan->epilogue;
   kp.beta = d.beta ? 1 : 0;
+  kp.a_mn = d.a_col_major ? 1 : 0;
+  kp.b_kmaj = d.b_col_major ? 1 : 0;
   kp.ex.bias = d.bias ? bias : nullptr;
   kp.ex.act = d.activation;
   kp.ex.clamp = d.clamp;

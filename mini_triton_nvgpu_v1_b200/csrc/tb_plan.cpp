@@ -102,6 +102,8 @@ extern "C" tbStatus tb_matmul_desc_init(tb_matmul_desc* d) {
   d->clamp = 0;
   d->clamp_lo = 0.f;
   d->clamp_hi = 0.f;
+  d->a_col_major = 0;
+  d->b_col_major = 0;
   return TB_OK;
 }
 
@@ -408,6 +410,8 @@ extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* bu
   o << "\"block_threads\": 192, ";
   o << "\"epilogue\": \"" << epi_names[plan->epilogue] << "\", ";
   o << "\"beta\": " << d.beta << ", ";
+  o << "\"a_layout\": \"" << (d.a_col_major ? "col_major" : "row_major") << "\", ";
+  o << "\"b_layout\": \"" << (d.b_col_major ? "col_major" : "row_major") << "\", ";
   {
     // the reference's EpilogueExprKind spelling, in application order
     const char* acts[] = {"", "activation(relu)", "activation(silu)", "activation(gelu_tanh)"};
