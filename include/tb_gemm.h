@@ -150,7 +150,9 @@ tbStatus tb_matmul_program_work(const tb_matmul_plan* plan, int64_t pid,
 /* Runs C = beta·C_in + A·B in place on `stream` (a cudaStream_t; NULL = the
  * legacy default stream). A is m×k row-major with row stride lda (elements),
  * B is k×n row-major with stride ldb, C is m×n row-major with stride ldc, of
- * c_dtype. lda and ldb must be multiples of 8 and A/B 16-byte aligned (TMA).
+ * c_dtype. TMA reads rows with 16-byte strides from 16-byte aligned bases;
+ * when the plan's row length is not a multiple of 8 elements, operands that
+ * break that rule are first copied, zero-padded, into the workspace.
  * `workspace` must hold tb_matmul_workspace_bytes(plan) bytes (may be NULL
  * when that is 0). Replaces kernel_tb_kernel_0(A, B, C) and its launch
  * (LowerPipelineToNVGPU.cpp:2678-2711; tools/bench_stage1_fair.py:67-74). */

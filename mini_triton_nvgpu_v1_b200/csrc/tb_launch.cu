@@ -740,6 +740,18 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// dst[r][c] = src[r][c] for c < cols, 0 for cols <= c < ld_dst (f16 rows).
+__global__ void __launch_bounds__(256)
+    tb_pack_rows_kernel(const uint16_t* __restrict__ src, int64_t ld_src, uint16_t* __restrict__ dst,
+                        int64_t ld_dst, int64_t rows, int64_t cols) {
+  const int64_t total = rows * ld_dst;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / ld_dst, c = i % ld_dst;
+    dst[i] = c < cols ? src[r * ld_src + c] : (uint16_t)0;
+  }
+}
+
 // ------------------------------------------------------------------ host
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
@@ -828,6 +840,20 @@ tbStatus dispatch_tile(const tb_matmul_plan* plan, const CUtensorMap& ta, const 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+tbStatus pack_rows_f16(const void* src, int64_t ld_src, void* dst, int64_t ld_dst, int64_t rows,
+                       int64_t cols, int num_sms, cudaStream_t stream) {
+  const int64_t total = rows * ld_dst;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > (int64_t)num_sms * 16) blocks = (int64_t)num_sms * 16;
+  if (blocks < 1) blocks = 1;
+  tb_pack_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint16_t*>(src), ld_src,
+                                                            static_cast<uint16_t*>(dst), ld_dst, rows,
+                                                            cols);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TB_OK
+                          : tb_fail(TB_ERR_CUDA, std::string("tb_pack_rows launch: ") + cudaGetErrorString(e));
+}
+
 }  // namespace
 
 size_t tb_kernel_smem_bytes(int32_t kernel_tile, int32_t /*stages*/) {
@@ -873,19 +899,45 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   // Likewise B (k × n): row-major ldb >= n, column-major ldb >= k.
   if (lda < (d.a_col_major ? d.m : d.k) || ldb < (d.b_col_major ? d.k : d.n) || ldc < d.n)
     return tb_fail(TB_ERR_INVALID_ARGUMENT, "leading dimensions must be >= the row length");
-  if (lda % 8 != 0 || ldb % 8 != 0)
+  // TMA reads rows whose stride is a multiple of 16 bytes from a 16-byte
+  // aligned base; other operands are first copied, zero-padded, into the
+  // plan's packing space in the workspace.
+  const bool pack_a = lda % 8 != 0 || !aligned16(A);
+  const bool pack_b = ldb % 8 != 0 || !aligned16(B);
+  if ((pack_a && !plan->pack_a_bytes) || (pack_b && !plan->pack_b_bytes))
     return tb_fail(TB_ERR_UNSUPPORTED,
-                   "lda and ldb must be multiples of 8 elements (16-byte TMA strides)");
-  if (!aligned16(A) || !aligned16(B))
-    return tb_fail(TB_ERR_UNSUPPORTED, "A and B must be 16-byte aligned (TMA)");
-  if (plan->workspace_bytes > 0 && (!workspace || workspace_bytes < plan->workspace_bytes))
-    return tb_fail(TB_ERR_WORKSPACE, "split_k_serial needs a workspace of " +
+                   "lda and ldb must be multiples of 8 elements and A, B 16-byte aligned "
+                   "(16-byte TMA strides); only plans whose row length is not a multiple of 8 "
+                   "reserve workspace to repack an operand");
+  const bool need_ws = plan->partial_bytes > 0 || pack_a || pack_b;
+  if (need_ws && (!workspace || workspace_bytes < plan->workspace_bytes))
+    return tb_fail(TB_ERR_WORKSPACE, "this run needs a workspace of " +
                                          std::to_string(plan->workspace_bytes) + " bytes");
   if (d.m > INT32_MAX || d.n > INT32_MAX || d.k > INT32_MAX)
     return tb_fail(TB_ERR_UNSUPPORTED, "problem dimensions must fit in 32 bits");
   tbStatus st = get_encoder();
   if (st != TB_OK) return st;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_v);
+
+  if (pack_a || pack_b) {
+    uint8_t* wsb = static_cast<uint8_t*>(workspace);
+    if (pack_a) {
+      const int64_t rows = d.a_col_major ? d.k : d.m, cols = d.a_col_major ? d.m : d.k;
+      const int64_t ld = (cols + 7) / 8 * 8;
+      st = pack_rows_f16(A, lda, wsb + plan->pack_a_offset, ld, rows, cols, plan->num_sms, stream);
+      if (st != TB_OK) return st;
+      A = wsb + plan->pack_a_offset;
+      lda = ld;
+    }
+    if (pack_b) {
+      const int64_t rows = d.b_col_major ? d.n : d.k, cols = d.b_col_major ? d.k : d.n;
+      const int64_t ld = (cols + 7) / 8 * 8;
+      st = pack_rows_f16(B, ldb, wsb + plan->pack_b_offset, ld, rows, cols, plan->num_sms, stream);
+      if (st != TB_OK) return st;
+      B = wsb + plan->pack_b_offset;
+      ldb = ld;
+    }
+  }
 
   CUtensorMap ta, tbm;
   if (d.a_col_major)  // storage k × m (m contiguous): [64 k × 64 m] boxes

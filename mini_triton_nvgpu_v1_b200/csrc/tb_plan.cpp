@@ -328,6 +328,21 @@ extern "C" tbStatus tb_matmul_plan_create(const tb_matmul_desc* desc, int device
     p.epilogue = kEpiStore;
     p.workspace_bytes = 0;
   }
+  // Operands whose contiguous rows are not a multiple of 8 elements (16 bytes)
+  // cannot be read by TMA in place: reserve room for a zero-padded copy.
+  {
+    auto align256 = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const int64_t a_rows = d.a_col_major ? d.k : d.m, a_cols = d.a_col_major ? d.m : d.k;
+    const int64_t b_rows = d.b_col_major ? d.n : d.k, b_cols = d.b_col_major ? d.k : d.n;
+    p.partial_bytes = p.workspace_bytes;
+    p.pack_a_bytes = a_cols % 8 ? (size_t)a_rows * (size_t)((a_cols + 7) / 8 * 8) * 2 : 0;
+    p.pack_b_bytes = b_cols % 8 ? (size_t)b_rows * (size_t)((b_cols + 7) / 8 * 8) * 2 : 0;
+    p.pack_a_offset = align256(p.partial_bytes);
+    p.pack_b_offset = p.pack_a_offset + align256(p.pack_a_bytes);
+    if (p.pack_b_bytes) p.workspace_bytes = p.pack_b_offset + p.pack_b_bytes;
+    else if (p.pack_a_bytes) p.workspace_bytes = p.pack_a_offset + p.pack_a_bytes;
+    else p.workspace_bytes = p.partial_bytes;
+  }
   // Resident program slots: one per SM, or one per SM pair for CTA pairs.
   const int64_t want = d.persistent ? p.resident_programs : total;
   const int64_t slots = std::max<int64_t>(1, num_sms / p.ctas_per_tile);

@@ -54,7 +54,10 @@ struct tb_matmul_plan {
   int64_t grid;                // CTAs launched
   size_t smem_bytes;
   int32_t tmem_cols;
-  size_t workspace_bytes;
+  size_t workspace_bytes;       // partial_bytes + pack_a_bytes + pack_b_bytes (256-aligned parts)
+  size_t partial_bytes;         // split_k_serial f32 partials, at offset 0
+  size_t pack_a_offset, pack_a_bytes;  // zero-padded copy of A when its rows are not TMA-aligned
+  size_t pack_b_offset, pack_b_bytes;  // same for B
 };
 
 // Defined in tb_launch.cu.
