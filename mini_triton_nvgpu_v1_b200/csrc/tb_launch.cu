@@ -51,7 +51,12 @@ __device__ uint32_t g_tb_status = 0;
 // [4] kernel cycles (per CTA, summed) [5] epilogue busy cycles
 __device__ unsigned long long g_tb_prof[8];
 #define TB_PROF_ADD(i, v) atomicAdd(&g_tb_prof[i], (unsigned long long)(v))
+// per-fill timestamps of CTA 0: [0] MMA commit issued, [1] producer saw
+// empty, [2] MMA saw full (fill index f = k-block count since start)
+__device__ long long g_tb_ts[3][512];
+#define TB_TS(which, f) do { if (blockIdx.x == 0 && (f) < 512) g_tb_ts[which][f] = clock64(); } while (0)
 #else
+#define TB_TS(which, f) ((void)0)
 #define TB_PROF_ADD(i, v) ((void)0)
 #endif
 
@@ -179,6 +184,11 @@ __device__ __forceinline__ bool wait_prof(uint32_t bar, uint32_t parity, volatil
 // Lane 0 waits (bounded), the result is broadcast so the warp stays converged.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           uint32_t site, int lane, long long& acc) {
+  // Every lane probes first with the non-blocking test_wait: in the common
+  // case (phase already complete) that is one probe, while a blocking
+  // try_wait costs hundreds of cycles even on a completed phase (measured:
+  // 142 → 118 cycles per MMA for a 128×128 tile, 154 → 132 for 128×256).
+  if (mbar_test_wait(bar, parity)) return true;
   int ok = 0;
   if (lane == 0) ok = wait_prof(bar, parity, abort_flag, site, 0, acc);
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
@@ -334,6 +344,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     long long issued = 0;
     long long prof_w = 0;
+#ifdef TB_EXP_NO_FULL_WAIT
+    if (false)
+#endif
     for (int32_t pid = first_pid; pid < p.map.total_programs; pid += pid_stride) {
       const Extent e = program_extent(p, pid);
       bool ok = true;
@@ -342,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        if (lane == 0) TB_TS(1, issued);
         const uint32_t fb_local = smem_addr(&full[stage]);
 #ifdef TB_DEBUG_NO_LOADS
         // Debug builds only: measure the MMA issue rate without operand traffic.
@@ -441,6 +455,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool issued_any = false;
       bool ok = true;
       long long prof_full = 0, prof_te = 0;
+#ifdef TB_WAIT_PROFILE
+      long long mma_fills = 0;
+#endif
       for (int32_t pid = first_pid; pid < p.map.total_programs && ok; pid += pid_stride) {
         const Extent e = program_extent(p, pid);
         if (!warp_wait(smem_addr(&tempty[acc]), acc_phase ^ 1u, abort_flag, kSiteMma, lane, prof_te)) break;
@@ -454,10 +471,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
         } else {
           for (int kb = 0; kb < e.nkb; ++kb) {
+#ifndef TB_EXP_NO_FULL_WAIT
             if (!warp_wait(smem_addr(&full[stage]), phase, abort_flag, kSiteMma, lane, prof_full)) {
               ok = false;
               break;
             }
+#endif
+            if (lane == 0) TB_TS(2, mma_fills);
             tc_fence_after();
             const int kvalid = min(kBK, e.k_end - (e.k_begin + kb * kBK));
             const uint32_t a0 = smem_addr(sA + (size_t)stage * kABytes);
@@ -471,10 +491,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                   // start-address field is bits [0,14) in 16-byte units
                   const uint64_t da = da0 + (uint64_t)((kk * a_step) >> 4);
                   const uint64_t db = db0 + (uint64_t)((kk * b_step) >> 4);
+#ifdef TB_EXP_ALT_ACC
+                  // debug experiment: alternate two accumulators (wrong results)
+                  const uint32_t dd = tmem_base + (uint32_t)(((acc ^ (kk & 1)) & 1) * BN);
+#else
+                  const uint32_t dd = d_tmem;
+#endif
                   if constexpr (G == 2)
-                    umma_f16_pair(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    umma_f16_pair(dd, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                   else
-                    umma_f16(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    umma_f16(dd, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                 }
               } else {
                 const int nk16 = (kvalid + 15) / 16;
@@ -487,11 +513,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_f16(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                 }
               }
+#if !defined(TB_EXP_NO_FULL_WAIT) || defined(TB_EXP_KEEP_COMMIT)
               if constexpr (G == 2) umma_commit_pair(smem_addr(&empty[stage]), 0x3);
               else umma_commit(smem_addr(&empty[stage]));
+#endif
+              TB_TS(0, mma_fills);
             }
             __syncwarp();
             issued_any = true;
+#ifdef TB_WAIT_PROFILE
+            ++mma_fills;
+#endif
             if (++stage == S) {
               stage = 0;
               phase ^= 1u;
@@ -1061,6 +1093,9 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
 }
 
 #ifdef TB_WAIT_PROFILE
+extern "C" int tb_debug_timestamps(long long* out) {
+  return cudaMemcpyFromSymbol(out, g_tb_ts, sizeof(g_tb_ts)) != cudaSuccess;
+}
 extern "C" int tb_debug_wait_profile(unsigned long long* out8, int reset) {
   if (cudaMemcpyFromSymbol(out8, g_tb_prof, sizeof(unsigned long long) * 8) != cudaSuccess) return 1;
   if (reset) {
