@@ -63,10 +63,7 @@ __device__ long long g_tb_ts[3][512];
 namespace {
 
 constexpr int kThreads = 192;
-constexpr int kBK = 64;               // K elements per ring stage (128-byte rows)
-constexpr int kCtaM = 128;            // tcgen05 M
-constexpr uint32_t kABytes = kCtaM * kBK * 2;
-constexpr uint32_t kBBoxBytes = 64 * kBK * 2;  // one [64 k × 64 n] box
+constexpr int kCtaM = 128;            // tcgen05 M per CTA
 constexpr size_t kSmemLimit = 232448;  // 227 KB opt-in per CTA
 constexpr long long kWaitBudgetCycles = 2000000000LL;  // ≈1 s at 1.9 GHz
 
@@ -75,10 +72,20 @@ constexpr uint32_t kSiteProducer = 1, kSiteMma = 2, kSiteEpilogue = 3, kSiteDrai
 // G = CTAs per tile: 1 (cta_group::1, 128-row tile) or 2 (cta_group::2 pair,
 // 256-row tile; each CTA holds 128 rows of A, BN/2 columns of B and 128
 // rows of the accumulator).
+// KB = K elements per ring stage: 64, or 128 when a CTA holds only 64 B
+// columns (its short MMA stages would otherwise be paced by the per-stage
+// barrier handshake; 8 MMAs per stage amortise it: measured −15 % time for
+// 128×64 and −9 % for the 256×128 pair at 8192³; 128×128 is L2-feed bound
+// and gains nothing).
 template <int BN, int G>
 struct Cfg {
   static constexpr int kBnCta = BN / G;                  // B columns per CTA
-  static constexpr uint32_t kBBytes = kBnCta * kBK * 2;  // kBnCta/64 boxes
+  static constexpr int kKB = kBnCta <= 64 ? 128 : 64;
+  static constexpr uint32_t kABytes = kCtaM * kKB * 2;   // KB/64 K-major [128 × 64] sub-tiles
+  static constexpr uint32_t kASub = kCtaM * 64 * 2;      // one K-major A sub-tile
+  static constexpr uint32_t kBoxBytes = 64 * kKB * 2;    // one MN-major [KB k × 64 mn] box
+  static constexpr uint32_t kBSub = kBnCta * 64 * 2;     // one K-major B sub-tile
+  static constexpr uint32_t kBBytes = kBnCta * kKB * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   // f32 output staging for the TMA-store epilogue: 4 warps × 2 buffers of
   // [32 rows × 32 f32] (128-byte swizzled rows).
@@ -198,7 +205,7 @@ struct Extent {
   int32_t m0, n0, rows, cols, k_begin, k_end, nkb, part;
 };
 
-__device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pid) {
+__device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pid, int32_t kb) {
   const tb::Work w = tb::program_work(p.map, pid);
   Extent e;
   e.m0 = w.tile_m * p.block_m;
@@ -207,7 +214,7 @@ __device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pid) 
   e.cols = min(p.block_n, p.N - e.n0);
   e.k_begin = w.kt_begin * p.block_k;
   e.k_end = min(p.K, (w.kt_begin + w.kt_count) * p.block_k);
-  e.nkb = e.k_end > e.k_begin ? (e.k_end - e.k_begin + kBK - 1) / kBK : 0;
+  e.nkb = e.k_end > e.k_begin ? (e.k_end - e.k_begin + kb - 1) / kb : 0;
   e.part = w.part;
   return e;
 }
@@ -287,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + (size_t)S * kABytes;
+  uint8_t* sB = smem + (size_t)S * Cf::kABytes;
   uint8_t* sEpi = sB + (size_t)S * Cf::kBBytes;  // 1024-aligned: stage sizes are multiples of 1 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + Cf::kEpiBytes);
   uint64_t* full = bars;            // leader: A/B of both CTAs landed
@@ -348,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (false)
 #endif
     for (int32_t pid = first_pid; pid < p.map.total_programs; pid += pid_stride) {
-      const Extent e = program_extent(p, pid);
+      const Extent e = program_extent(p, pid, Cf::kKB);
       bool ok = true;
       for (int kb = 0; kb < e.nkb; ++kb) {
         if (!warp_wait(smem_addr(&empty[stage]), phase ^ 1u, abort_flag, kSiteProducer, lane, prof_w)) {
@@ -368,8 +375,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         continue;
 #endif
-        const int32_t kx = e.k_begin + kb * kBK;
-        const uint32_t dA = smem_addr(sA + (size_t)stage * kABytes);
+        const int32_t kx = e.k_begin + kb * Cf::kKB;
+        const uint32_t dA = smem_addr(sA + (size_t)stage * Cf::kABytes);
         const uint32_t dB = smem_addr(sB + (size_t)stage * Cf::kBBytes);
         if (elect_one()) {
           if (leader) mbar_expect_tx(fb_local, G * Cf::kStageBytes);
@@ -377,32 +384,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t fb = map_to_cta(fb_local, 0);
             const int32_t am = e.m0 + (int32_t)rank * 128;
             const int32_t bn = e.n0 + (int32_t)rank * Cf::kBnCta;
-            if (p.a_mn) {  // two [64 k × 64 m] boxes
+            if (p.a_mn) {  // two [KB k × 64 m] boxes
               tma_load_2d_pair(dA, &tmA, fb, am, kx);
-              tma_load_2d_pair(dA + kBBoxBytes, &tmA, fb, am + 64, kx);
-            } else {
-              tma_load_2d_pair(dA, &tmA, fb, kx, am);
+              tma_load_2d_pair(dA + Cf::kBoxBytes, &tmA, fb, am + 64, kx);
+            } else {       // KB/64 [128 m × 64 k] sub-tiles
+#pragma unroll
+              for (int j = 0; j < Cf::kKB / 64; ++j)
+                tma_load_2d_pair(dA + j * Cf::kASub, &tmA, fb, kx + 64 * j, am);
             }
-            if (p.b_kmaj) {  // one [kBnCta n × 64 k] box
-              tma_load_2d_pair(dB, &tmB, fb, kx, bn);
-            } else {
+            if (p.b_kmaj) {  // KB/64 [kBnCta n × 64 k] sub-tiles
+#pragma unroll
+              for (int j = 0; j < Cf::kKB / 64; ++j)
+                tma_load_2d_pair(dB + j * Cf::kBSub, &tmB, fb, kx + 64 * j, bn);
+            } else {         // kBnCta/64 [KB k × 64 n] boxes
 #pragma unroll
               for (int j = 0; j < Cf::kBnCta / 64; ++j)
-                tma_load_2d_pair(dB + j * kBBoxBytes, &tmB, fb, bn + 64 * j, kx);
+                tma_load_2d_pair(dB + j * Cf::kBoxBytes, &tmB, fb, bn + 64 * j, kx);
             }
           } else {
             if (p.a_mn) {
               tma_load_2d(dA, &tmA, fb_local, e.m0, kx);
-              tma_load_2d(dA + kBBoxBytes, &tmA, fb_local, e.m0 + 64, kx);
+              tma_load_2d(dA + Cf::kBoxBytes, &tmA, fb_local, e.m0 + 64, kx);
             } else {
-              tma_load_2d(dA, &tmA, fb_local, kx, e.m0);
+#pragma unroll
+              for (int j = 0; j < Cf::kKB / 64; ++j)
+                tma_load_2d(dA + j * Cf::kASub, &tmA, fb_local, kx + 64 * j, e.m0);
             }
             if (p.b_kmaj) {
-              tma_load_2d(dB, &tmB, fb_local, kx, e.n0);
+#pragma unroll
+              for (int j = 0; j < Cf::kKB / 64; ++j)
+                tma_load_2d(dB + j * Cf::kBSub, &tmB, fb_local, kx + 64 * j, e.n0);
             } else {
 #pragma unroll
               for (int j = 0; j < Cf::kBnCta / 64; ++j)
-                tma_load_2d(dB + j * kBBoxBytes, &tmB, fb_local, e.n0 + 64 * j, kx);
+                tma_load_2d(dB + j * Cf::kBoxBytes, &tmB, fb_local, e.n0 + 64 * j, kx);
             }
           }
         }
@@ -442,12 +457,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (leader) {
       const uint32_t idesc = idesc_f16_f32(kCtaM * G, BN, p.a_mn ? 1 : 0, p.b_kmaj ? 0 : 1);
       // Per-operand layout in shared memory (all 128-byte swizzled):
-      //   K-major: rows of 64 k (128 B), 8-row groups 1024 B apart (SBO); a
-      //            K step of 16 elements is 32 B inside the swizzle atom.
-      //   MN-major: [64 k × 64 mn] boxes kBBoxBytes apart (LBO), 8 k-rows
+      //   K-major: sub-tiles of rows of 64 k (128 B), 8-row groups 1024 B
+      //            apart (SBO); a K step of 16 elements is 32 B inside the
+      //            swizzle atom, every 4th step moves to the next sub-tile.
+      //   MN-major: [KB k × 64 mn] boxes kBoxBytes apart (LBO), 8 k-rows
       //            1024 B apart (SBO); a K step of 16 rows is 2048 B.
-      const uint32_t a_lbo = p.a_mn ? kBBoxBytes : 16u, a_step = p.a_mn ? 2048u : 32u;
-      const uint32_t b_lbo = p.b_kmaj ? 16u : kBBoxBytes, b_step = p.b_kmaj ? 32u : 2048u;
+      const uint32_t a_lbo = p.a_mn ? Cf::kBoxBytes : 16u;
+      const uint32_t b_lbo = p.b_kmaj ? 16u : Cf::kBoxBytes;
+      auto a_off = [&](int kk) -> uint32_t {
+        return p.a_mn ? (uint32_t)kk * 2048u : (uint32_t)(kk >> 2) * Cf::kASub + (uint32_t)(kk & 3) * 32u;
+      };
+      auto b_off = [&](int kk) -> uint32_t {
+        return p.b_kmaj ? (uint32_t)(kk >> 2) * Cf::kBSub + (uint32_t)(kk & 3) * 32u : (uint32_t)kk * 2048u;
+      };
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -459,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       long long mma_fills = 0;
 #endif
       for (int32_t pid = first_pid; pid < p.map.total_programs && ok; pid += pid_stride) {
-        const Extent e = program_extent(p, pid);
+        const Extent e = program_extent(p, pid, Cf::kKB);
         if (!warp_wait(smem_addr(&tempty[acc]), acc_phase ^ 1u, abort_flag, kSiteMma, lane, prof_te)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -479,18 +501,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
             if (lane == 0) TB_TS(2, mma_fills);
             tc_fence_after();
-            const int kvalid = min(kBK, e.k_end - (e.k_begin + kb * kBK));
-            const uint32_t a0 = smem_addr(sA + (size_t)stage * kABytes);
+            const int kvalid = min(Cf::kKB, e.k_end - (e.k_begin + kb * Cf::kKB));
+            const uint32_t a0 = smem_addr(sA + (size_t)stage * Cf::kABytes);
             const uint32_t b0 = smem_addr(sB + (size_t)stage * Cf::kBBytes);
             const uint64_t da0 = smem_desc_sw128(a0, a_lbo, 1024);
             const uint64_t db0 = smem_desc_sw128(b0, b_lbo, 1024);
             if (elect_one()) {
-              if (kvalid == kBK) {
+              if (kvalid == Cf::kKB) {
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk) {
+                for (int kk = 0; kk < Cf::kKB / 16; ++kk) {
                   // start-address field is bits [0,14) in 16-byte units
-                  const uint64_t da = da0 + (uint64_t)((kk * a_step) >> 4);
-                  const uint64_t db = db0 + (uint64_t)((kk * b_step) >> 4);
+                  const uint64_t da = da0 + (uint64_t)(a_off(kk) >> 4);
+                  const uint64_t db = db0 + (uint64_t)(b_off(kk) >> 4);
 #ifdef TB_EXP_ALT_ACC
                   // debug experiment: alternate two accumulators (wrong results)
                   const uint32_t dd = tmem_base + (uint32_t)(((acc ^ (kk & 1)) & 1) * BN);
@@ -505,8 +527,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               } else {
                 const int nk16 = (kvalid + 15) / 16;
                 for (int kk = 0; kk < nk16; ++kk) {
-                  const uint64_t da = da0 + (uint64_t)((kk * a_step) >> 4);
-                  const uint64_t db = db0 + (uint64_t)((kk * b_step) >> 4);
+                  const uint64_t da = da0 + (uint64_t)(a_off(kk) >> 4);
+                  const uint64_t db = db0 + (uint64_t)(b_off(kk) >> 4);
                   if constexpr (G == 2)
                     umma_f16_pair(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                   else
@@ -568,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     long long prof_tf = 0;
     for (int32_t pid = first_pid; pid < p.map.total_programs; pid += pid_stride) {
-      const Extent e = program_extent(p, pid);
+      const Extent e = program_extent(p, pid, Cf::kKB);
       int ok = 0;
       if (lane == 0) ok = wait_prof(smem_addr(&tfull[acc]), acc_phase, abort_flag, kSiteEpilogue, 3, prof_tf);
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -899,6 +921,17 @@ size_t tb_kernel_smem_bytes(int32_t kernel_tile, int32_t /*stages*/) {
   return 0;
 }
 
+int32_t tb_kernel_kb(int32_t kernel_tile) {
+  switch (kernel_tile) {
+    case kTile128x64: return Cfg<64, 1>::kKB;
+    case kTile128x128: return Cfg<128, 1>::kKB;
+    case kTile128x256: return Cfg<256, 1>::kKB;
+    case kTile256x128: return Cfg<128, 2>::kKB;
+    case kTile256x256: return Cfg<256, 2>::kKB;
+  }
+  return 0;
+}
+
 int32_t tb_kernel_max_stages(int32_t kernel_tile) {
   switch (kernel_tile) {
     case kTile128x64: return Cfg<64, 1>::kStages;
@@ -973,14 +1006,14 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
 
   CUtensorMap ta, tbm;
   if (d.a_col_major)  // storage k × m (m contiguous): [64 k × 64 m] boxes
-    st = encode_f16_2d(&ta, A, d.k, d.m, lda, kBK, "A");
+    st = encode_f16_2d(&ta, A, d.k, d.m, lda, (uint32_t)plan->kb, "A");
   else                // storage m × k: [128 m × 64 k] boxes
     st = encode_f16_2d(&ta, A, d.m, d.k, lda, kCtaM, "A");
   if (st != TB_OK) return st;
   if (d.b_col_major)  // storage n × k (k contiguous): [BN/G n × 64 k] boxes
     st = encode_f16_2d(&tbm, B, d.n, d.k, ldb, (uint32_t)(plan->cta_n / plan->ctas_per_tile), "B");
   else                // storage k × n: [64 k × 64 n] boxes
-    st = encode_f16_2d(&tbm, B, d.k, d.n, ldb, kBK, "B");
+    st = encode_f16_2d(&tbm, B, d.k, d.n, ldb, (uint32_t)plan->kb, "B");
   if (st != TB_OK) return st;
 
   const size_t out_bytes = d.c_dtype == TB_F16 ? 2 : 4;

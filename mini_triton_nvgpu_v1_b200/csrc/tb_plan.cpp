@@ -301,6 +301,7 @@ extern "C" tbStatus tb_matmul_plan_create(const tb_matmul_desc* desc, int device
   // tb.requested-stages.
   p.stages = std::max<int32_t>((int32_t)d.num_stages, tb_kernel_max_stages(p.kernel_tile));
   p.smem_bytes = tb_kernel_smem_bytes(p.kernel_tile, p.stages);
+  p.kb = tb_kernel_kb(p.kernel_tile);
   p.tmem_cols = 2 * p.cta_n;  // two accumulators (epilogue/mainloop overlap)
 
   if (d.activation < TB_ACT_NONE || d.activation > TB_ACT_GELU_TANH)
@@ -416,7 +417,7 @@ extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* bu
   o << "\"selected_mainline_kind\": \"" << plan->mainline_kind << "\", ";
   o << "\"num_sms\": " << plan->num_sms << ", ";
   o << "\"kernel\": \"" << kernel_names[plan->kernel_tile] << "\", ";
-  o << "\"cta_tile\": [" << plan->cta_m << ", " << plan->cta_n << ", 64], ";
+  o << "\"cta_tile\": [" << plan->cta_m << ", " << plan->cta_n << ", " << plan->kb << "], ";
   o << "\"ctas_per_tile\": " << plan->ctas_per_tile << ", ";
   o << "\"stages\": " << plan->stages << ", ";
   o << "\"smem_bytes\": " << plan->smem_bytes << ", ";

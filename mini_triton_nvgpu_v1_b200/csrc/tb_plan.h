@@ -49,7 +49,8 @@ struct tb_matmul_plan {
   int32_t kernel_tile;         // TbKernelTile
   int32_t cta_m, cta_n;        // hardware tile (cta_m = 256: a CTA pair)
   int32_t ctas_per_tile;       // 1 or 2
-  int32_t stages;              // shared-memory ring depth (64-deep K stages)
+  int32_t stages;              // shared-memory ring depth
+  int32_t kb;                  // K elements per ring stage (64 or 128)
   int32_t epilogue;            // TbEpilogue
   int64_t grid;                // CTAs launched
   size_t smem_bytes;
@@ -69,6 +70,7 @@ tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda,
                    void* workspace, size_t workspace_bytes, void* stream);
 size_t tb_kernel_smem_bytes(int32_t kernel_tile, int32_t stages);
 int32_t tb_kernel_max_stages(int32_t kernel_tile);
+int32_t tb_kernel_kb(int32_t kernel_tile);
 
 // Thread-local error message helpers (tb_plan.cpp).
 tbStatus tb_fail(tbStatus code, const std::string& msg);
