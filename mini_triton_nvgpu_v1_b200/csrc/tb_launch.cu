@@ -351,9 +351,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     long long issued = 0;
     long long prof_w = 0;
-#ifdef TB_EXP_NO_FULL_WAIT
-    if (false)
-#endif
     for (int32_t pid = first_pid; pid < p.map.total_programs; pid += pid_stride) {
       const Extent e = program_extent(p, pid, Cf::kKB);
       bool ok = true;
@@ -493,12 +490,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
         } else {
           for (int kb = 0; kb < e.nkb; ++kb) {
-#ifndef TB_EXP_NO_FULL_WAIT
             if (!warp_wait(smem_addr(&full[stage]), phase, abort_flag, kSiteMma, lane, prof_full)) {
               ok = false;
               break;
             }
-#endif
             if (lane == 0) TB_TS(2, mma_fills);
             tc_fence_after();
             const int kvalid = min(Cf::kKB, e.k_end - (e.k_begin + kb * Cf::kKB));
@@ -513,12 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   // start-address field is bits [0,14) in 16-byte units
                   const uint64_t da = da0 + (uint64_t)(a_off(kk) >> 4);
                   const uint64_t db = db0 + (uint64_t)(b_off(kk) >> 4);
-#ifdef TB_EXP_ALT_ACC
-                  // debug experiment: alternate two accumulators (wrong results)
-                  const uint32_t dd = tmem_base + (uint32_t)(((acc ^ (kk & 1)) & 1) * BN);
-#else
                   const uint32_t dd = d_tmem;
-#endif
                   if constexpr (G == 2)
                     umma_f16_pair(dd, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                   else
@@ -535,10 +525,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_f16(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                 }
               }
-#if !defined(TB_EXP_NO_FULL_WAIT) || defined(TB_EXP_KEEP_COMMIT)
               if constexpr (G == 2) umma_commit_pair(smem_addr(&empty[stage]), 0x3);
               else umma_commit(smem_addr(&empty[stage]));
-#endif
               TB_TS(0, mma_fills);
             }
             __syncwarp();
