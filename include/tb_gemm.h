@@ -233,6 +233,13 @@ tbStatus tb_matmul(const tb_matmul_desc* desc, const void* A, int64_t lda,
  * has no device-side failure detection; this has no counterpart there. */
 tbStatus tb_device_status(void* stream, uint32_t* raw_status);
 
+/* Failure-detection self-test: launches one warp that waits, bounded by
+ * `budget_cycles` SM clocks (at most 2e9), on an mbarrier nothing arrives on,
+ * using the GEMM kernels' bounded-wait and status-recording code. Afterwards
+ * tb_device_status() reports TB_ERR_DEVICE_TIMEOUT (site 5) and the context
+ * stays usable. No counterpart in the reference. */
+tbStatus tb_selftest_bounded_wait(void* stream, uint64_t budget_cycles);
+
 /* Message of the calling thread's most recent failure ("" if none). */
 const char* tb_last_error(void);
 

@@ -96,6 +96,7 @@ PROTOTYPES = {
                                             C.c_int64, C.c_void_p]),
     "tb_peer_comm_status": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_uint32)]),
     "tb_peer_comm_destroy": (C.c_int, [C.c_void_p]),
+    "tb_selftest_bounded_wait": (C.c_int, [C.c_void_p, C.c_uint64]),
     "tb_device_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32)]),
     "tb_last_error": (C.c_char_p, []),
     "tb_version": (C.c_char_p, []),

@@ -67,7 +67,8 @@ constexpr int kCtaM = 128;            // tcgen05 M per CTA
 constexpr size_t kSmemLimit = 232448;  // 227 KB opt-in per CTA
 constexpr long long kWaitBudgetCycles = 2000000000LL;  // ≈1 s at 1.9 GHz
 
-constexpr uint32_t kSiteProducer = 1, kSiteMma = 2, kSiteEpilogue = 3, kSiteDrain = 4;
+constexpr uint32_t kSiteProducer = 1, kSiteMma = 2, kSiteEpilogue = 3, kSiteDrain = 4,
+                   kSiteSelfTest = 5;
 
 // G = CTAs per tile: 1 (cta_group::1, 128-row tile) or 2 (cta_group::2 pair,
 // 256-row tile; each CTA holds 128 rows of A, BN/2 columns of B and 128
@@ -1183,6 +1184,37 @@ extern "C" tbStatus tb_matmul_run_no_alloc(const tb_matmul_plan* plan, const voi
   // Every split part writes all of its m x n partial plane before the
   // reduction reads it, so the scratch needs no clearing between calls.
   return tb_launch(plan, A, lda, B, ldb, C, ldc, scratch, need > 0 ? kNoAllocScratchBytes : 0, stream);
+}
+
+// Self-test of the failure-detection path: one warp waits, bounded by
+// `budget` cycles, on an mbarrier nothing ever arrives on — the same probe,
+// budget check and status recording the GEMM's waits use — then returns.
+__global__ void tb_selftest_wait_kernel(long long budget) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_addr(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(smem_addr(&bar), 0)) {
+      if (clock64() - t0 > budget) {
+        record_error(TB_ERR_DEVICE_TIMEOUT, kSiteSelfTest);
+        break;
+      }
+    }
+  }
+}
+
+extern "C" tbStatus tb_selftest_bounded_wait(void* stream, uint64_t budget_cycles) {
+  tb_clear_error();
+  if (budget_cycles == 0 || budget_cycles > (uint64_t)kWaitBudgetCycles)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "budget_cycles must be in (0, 2e9]");
+  tb_selftest_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>((long long)budget_cycles);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TB_OK
+                          : tb_fail(TB_ERR_CUDA, std::string("tb_selftest launch: ") + cudaGetErrorString(e));
 }
 
 extern "C" tbStatus tb_device_status(void* stream, uint32_t* raw) {
