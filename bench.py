@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "splitk"],
+    ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "splitk", "sweep"],
                     help="gemm8192: the headline 8192^3 N-sharded GEMM; splitk: the skinny "
                          "512x512x65536 split-K config (K-sharded + reduce-scatter at N>1)")
     ap.add_argument("--kshard", default="peer", choices=["peer", "nccl"],
@@ -466,12 +466,126 @@ def run_splitk(args):
     return 0
 
 
+# Every BASELINE config on one GPU: (name, m, n, k, knobs, c dtype, bound).
+SWEEP = [
+    ("smoke 64x64x32 (tile 64x64x32, 4 warps)", 64, 64, 32,
+     dict(block_m=64, block_n=64, block_k=32, num_warps=4), "f32", "latency"),
+    ("ragged 96x80x32 (tile 128x128x64, f16 out)", 96, 80, 32,
+     dict(block_m=128, block_n=128, block_k=64, exact_tile=False), "f16", "latency"),
+    ("ragged scale-up 4096^3 (tile 128x128x64, f16 out)", 4096, 4096, 4096,
+     dict(block_m=128, block_n=128, block_k=64), "f16", "tensor"),
+    ("grouped 192x128x32 (tile 64x64x32, GROUP_M=8)", 192, 128, 32,
+     dict(block_m=64, block_n=64, block_k=32, group_m=8), "f32", "latency"),
+    ("grouped 8192^3 (GROUP_M=8, pair 256x256)", 8192, 8192, 8192,
+     dict(block_m=256, block_n=256, block_k=64, group_m=8), "f32", "tensor"),
+    ("split-K 64x64x64 (split 2)", 64, 64, 64,
+     dict(block_m=64, block_n=64, block_k=32, split_k=2, reduction_mode="split_k_serial"), "f32", "latency"),
+    ("split-K 512x512x65536 (split 16, serial)", 512, 512, 65536,
+     dict(block_m=256, block_n=256, block_k=64, split_k=16, reduction_mode="split_k_serial"), "f32", "hbm"),
+    ("split-K 512x512x65536 (split 16, parallel)", 512, 512, 65536,
+     dict(block_m=256, block_n=256, block_k=64, split_k=16, reduction_mode="split_k_parallel"), "f32", "hbm"),
+    ("persistent 192x128x32 (num_ctas=2)", 192, 128, 32,
+     dict(block_m=64, block_n=64, block_k=32, persistent=True, num_ctas=2), "f16", "latency"),
+    ("persistent 2048^3 (pair, grid=SMs, f16 out)", 2048, 2048, 2048,
+     dict(block_m=256, block_n=256, block_k=64, persistent=True, num_ctas=148), "f16", "tensor"),
+    ("persistent 8192^3 (pair, grid=SMs, f16 out)", 8192, 8192, 8192,
+     dict(block_m=256, block_n=256, block_k=64, persistent=True, num_ctas=148), "f16", "tensor"),
+    ("persistent 16384^3 (pair, grid=SMs, f16 out)", 16384, 16384, 16384,
+     dict(block_m=256, block_n=256, block_k=64, persistent=True, num_ctas=148), "f16", "tensor"),
+]
+
+
+def run_sweep(args):
+    """One JSON line per BASELINE config: device time per call (CUDA events,
+    ~0.3 s of back-to-back calls after warm-up, best of 3), TFLOP/s and the
+    fraction of the roofline that bounds the config."""
+    import torch
+    import mini_triton_nvgpu_v1_b200 as tb
+    dev = torch.device("cuda", 0)
+    peak_b, peak_s, _ = peaks()
+    hbm = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("hbm_gbs", 6650.0) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 6650.0
+    for name, m, n, k, kn, cdt, bound in SWEEP:
+        g = torch.Generator(device=dev).manual_seed(2)
+        A = (torch.rand(m, k, device=dev, generator=g) * 2 - 1).half()
+        B = (torch.rand(k, n, device=dev, generator=g) * 2 - 1).half()
+        C = torch.zeros(m, n, device=dev, dtype=torch.float16 if cdt == "f16" else torch.float32)
+        ws = None
+        f = lambda: tb.matmul(A, B, C, workspace=ws, **kn)
+        for _ in range(5):
+            f()
+        torch.cuda.synchronize()
+        t0 = time.time()
+        n_ = 0
+        while time.time() - t0 < 0.05:
+            f()
+            n_ += 1
+        torch.cuda.synchronize()
+        reps = max(10, int(0.3 / ((time.time() - t0) / n_)))
+        best = 1e30
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                f()
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1) / reps)
+        tb.device_status()
+        # device-only time per call: replay a CUDA graph of back-to-back calls
+        graph_us = None
+        try:
+            if ws is None and kn.get("split_k", 1) > 1 and kn.get("reduction_mode") == "split_k_serial":
+                ws = torch.empty(tb.MatmulPlan(tb.KernelConfig(m=m, n=n, k=k, c_dtype=cdt, **{
+                    kk: v for kk, v in kn.items()}), 0).workspace_bytes, dtype=torch.uint8, device=dev)
+            gr = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                f()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            n_g = 20
+            with torch.cuda.graph(gr):
+                for _ in range(n_g):
+                    f()
+            gr.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps_g = max(3, int(reps / n_g))
+            e0.record()
+            for _ in range(reps_g):
+                gr.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            graph_us = round(e0.elapsed_time(e1) / (reps_g * n_g) * 1e3, 2)
+            del gr
+        except Exception as exc:  # capture unsupported: report the eager number only
+            graph_us = f"capture failed: {type(exc).__name__}"
+        tb.device_status()
+        flops = 2.0 * m * n * k
+        cb = 2 if cdt == "f16" else 4
+        alg_bytes = 2.0 * (m * k + k * n) + 2 * cb * m * n
+        line = {"workload": "sweep", "config": name, "us": round(best * 1e3, 2), "graph_us": graph_us,
+                "tflops": round(flops / (best * 1e-3) / 1e12, 2),
+                "gbs": round(alg_bytes / (best * 1e-3) / 1e9, 1), "bound": bound}
+        if bound == "tensor":
+            line["frac_of_sustained_peak"] = round(line["tflops"] / peak_s, 3)
+        elif bound == "hbm":
+            line["frac_of_hbm"] = round(line["gbs"] / hbm, 3)
+        print(json.dumps(line), flush=True)
+        del A, B, C
+        torch.cuda.empty_cache()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "splitk":
         return run_splitk(args)
+    if args.workload == "sweep":
+        return run_sweep(args)
     return run_ours(args)
 
 

@@ -814,6 +814,57 @@ tbStatus get_encoder() {
   return TB_OK;
 }
 
+// Encoding a tensor map costs ~1 µs of host time per operand; repeated calls
+// on the same buffers reuse it. The cache is per host thread (no locking) and
+// keyed by every encode argument, so a hit always equals a fresh encode.
+struct MapKey {
+  int dtype, rank, swizzle;
+  const void* base;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool used;
+};
+constexpr int kMapCacheSize = 8;
+thread_local MapEntry t_map_cache[kMapCacheSize];
+thread_local int t_map_next = 0;
+
+CUresult encode_cached(CUtensorMap* out, CUtensorMapDataType dtype, int rank, void* base,
+                       const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                       CUtensorMapSwizzle swizzle, CUtensorMapL2promotion l2) {
+  MapKey k;
+  std::memset(&k, 0, sizeof(k));
+  k.dtype = (int)dtype;
+  k.rank = rank;
+  k.swizzle = (int)swizzle | ((int)l2 << 8);
+  k.base = base;
+  for (int i = 0; i < rank; ++i) {
+    k.dims[i] = dims[i];
+    k.box[i] = box[i];
+  }
+  for (int i = 0; i + 1 < rank; ++i) k.strides[i] = strides[i];
+  for (int i = 0; i < kMapCacheSize; ++i) {
+    if (t_map_cache[i].used && std::memcmp(&t_map_cache[i].key, &k, sizeof(k)) == 0) {
+      *out = t_map_cache[i].map;
+      return CUDA_SUCCESS;
+    }
+  }
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(out, dtype, (cuuint32_t)rank, base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_SUCCESS) {
+    MapEntry& e = t_map_cache[t_map_next];
+    t_map_next = (t_map_next + 1) % kMapCacheSize;
+    e.key = k;
+    e.map = *out;
+    e.used = true;
+  }
+  return r;
+}
+
 // Row-major f16 matrix rows × cols with row stride ld (elements), boxed
 // [box_rows × 64] with 128-byte swizzle; out-of-range elements read as 0.
 tbStatus encode_f16_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
@@ -821,11 +872,8 @@ tbStatus encode_f16_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
   cuuint32_t box[2] = {64, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_cached(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                             strides, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (r != CUDA_SUCCESS)
     return tb_fail(TB_ERR_CUDA, std::string("cuTensorMapEncodeTiled(") + what +
                                     ") failed with CUresult " + std::to_string((int)r));
@@ -1052,20 +1100,17 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
     kp.tma_out = kTmaStoreWs;
   if (kp.tma_out != kTmaNone) {
     cuuint32_t box[3] = {32, 32, 1};
-    cuuint32_t estr[3] = {1, 1, 1};
     CUresult r;
     if (kp.tma_out == kTmaStoreWs) {
       cuuint64_t dims[3] = {(cuuint64_t)d.n, (cuuint64_t)d.m, (cuuint64_t)kp.map.split_k};
       cuuint64_t strides[2] = {(cuuint64_t)d.n * 4, (cuuint64_t)d.m * (cuuint64_t)d.n * 4};
-      r = g_encode(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, workspace, dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      r = encode_cached(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, workspace, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
     } else {
       cuuint64_t dims[2] = {(cuuint64_t)d.n, (cuuint64_t)d.m};
       cuuint64_t strides[1] = {(cuuint64_t)ldc * 4};
-      r = g_encode(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Cp, dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      r = encode_cached(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, Cp, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
     }
     if (r != CUDA_SUCCESS)
       return tb_fail(TB_ERR_CUDA, "cuTensorMapEncodeTiled(C) failed with CUresult " +
