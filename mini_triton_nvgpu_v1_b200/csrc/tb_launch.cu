@@ -146,6 +146,8 @@ struct KParams {
   int32_t vec_c;     // C rows allow 16-byte vector access
   int32_t vec_ws;    // workspace rows allow 16-byte vector access
   int32_t tma_out;   // TmaOut: f32 tile output written by TMA from swizzled shared staging
+  int32_t fuse;      // program pairing (plan.fuse): work item w runs programs 2w and 2w+1
+  int32_t work_items;
   EpiExprs ex;       // applied in kEpiStore (split_k_serial: in the reduction)
   int32_t a_mn;      // A stored M-major (column-major m × k): MN-major UMMA operand
   int32_t b_kmaj;    // B stored K-major (column-major k × n): K-major UMMA operand
@@ -207,12 +209,12 @@ struct Extent {
 };
 
 __device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pid, int32_t kb) {
-  const tb::Work w = tb::program_work(p.map, pid);
+  const tb::Work w = tb::program_work(p.map, p.fuse ? 2 * pid : pid);
   Extent e;
   e.m0 = w.tile_m * p.block_m;
   e.n0 = w.tile_n * p.block_n;
-  e.rows = min(p.block_m, p.M - e.m0);
-  e.cols = min(p.block_n, p.N - e.n0);
+  e.rows = min(p.block_m * (p.fuse == 1 ? 2 : 1), p.M - e.m0);
+  e.cols = min(p.block_n * (p.fuse == 2 ? 2 : 1), p.N - e.n0);
   e.k_begin = w.kt_begin * p.block_k;
   e.k_end = min(p.K, (w.kt_begin + w.kt_count) * p.block_k);
   e.nkb = e.k_end > e.k_begin ? (e.k_end - e.k_begin + kb - 1) / kb : 0;
@@ -352,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     long long issued = 0;
     long long prof_w = 0;
-    for (int32_t pid = first_pid; pid < p.map.total_programs; pid += pid_stride) {
+    for (int32_t pid = first_pid; pid < p.work_items; pid += pid_stride) {
       const Extent e = program_extent(p, pid, Cf::kKB);
       bool ok = true;
       for (int kb = 0; kb < e.nkb; ++kb) {
@@ -478,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef TB_WAIT_PROFILE
       long long mma_fills = 0;
 #endif
-      for (int32_t pid = first_pid; pid < p.map.total_programs && ok; pid += pid_stride) {
+      for (int32_t pid = first_pid; pid < p.work_items && ok; pid += pid_stride) {
         const Extent e = program_extent(p, pid, Cf::kKB);
         if (!warp_wait(smem_addr(&tempty[acc]), acc_phase ^ 1u, abort_flag, kSiteMma, lane, prof_te)) break;
         tc_fence_after();
@@ -578,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     long long prof_tf = 0;
-    for (int32_t pid = first_pid; pid < p.map.total_programs; pid += pid_stride) {
+    for (int32_t pid = first_pid; pid < p.work_items; pid += pid_stride) {
       const Extent e = program_extent(p, pid, Cf::kKB);
       int ok = 0;
       if (lane == 0) ok = wait_prof(smem_addr(&tfull[acc]), acc_phase, abort_flag, kSiteEpilogue, 3, prof_tf);
@@ -1064,6 +1066,8 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   kp.block_k = (int32_t)d.block_k;
   kp.epilogue = plan->epilogue;
   kp.beta = d.beta ? 1 : 0;
+  kp.fuse = plan->fuse;
+  kp.work_items = (int32_t)plan->work_items;
   kp.a_mn = d.a_col_major ? 1 : 0;
   kp.b_kmaj = d.b_col_major ? 1 : 0;
   kp.ex.bias = d.bias ? bias : nullptr;
@@ -1091,7 +1095,8 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   CUtensorMap tcm;
   memset(&tcm, 0, sizeof(tcm));
   kp.tma_out = kTmaNone;
-  const bool exact_hw_tile = d.block_m == plan->cta_m && d.block_n == plan->cta_n;
+  const bool exact_hw_tile = d.block_m * (plan->fuse == 1 ? 2 : 1) == plan->cta_m &&
+                             d.block_n * (plan->fuse == 2 ? 2 : 1) == plan->cta_n;
   if (exact_hw_tile && d.c_dtype == TB_F32 && aligned16(Cp) && ldc % 4 == 0) {
     if (plan->epilogue == kEpiStore) kp.tma_out = kTmaStoreC;
     if (plan->epilogue == kEpiAtomic) kp.tma_out = kTmaReduceC;

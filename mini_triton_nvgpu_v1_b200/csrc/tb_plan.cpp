@@ -285,16 +285,32 @@ extern "C" tbStatus tb_matmul_plan_create(const tb_matmul_desc* desc, int device
   if (d.block_n > 256)
     return tb_fail(TB_ERR_UNSUPPORTED,
                    "block_n > 256 is not supported (tcgen05 N <= 256)");
-  if (d.block_m <= 128) {
+  // Consecutive program ids in grouped order are vertically adjacent tiles
+  // (LowerPipelineToNVGPU.cpp:283-304: tile_m advances fastest inside a
+  // group), and in row-major / persistent order horizontally adjacent. When
+  // every such pair is aligned, two programs share one hardware tile (half
+  // the operand traffic per FLOP); a 32-bit program walk stays the same.
+  p.fuse = 0;
+  if (split_k == 1 && total % 2 == 0) {
+    if (kind == tb::kMapGroupedTile && span_m % 2 == 0 && tiles_m % 2 == 0 && 2 * d.block_m <= 256)
+      p.fuse = 1;
+    else if ((kind == tb::kMapTile || kind == tb::kMapPersistentTile) && tiles_n % 2 == 0 &&
+             2 * d.block_n <= 256)
+      p.fuse = 2;
+  }
+  p.work_items = p.fuse ? total / 2 : total;
+  const int64_t eff_bm = d.block_m * (p.fuse == 1 ? 2 : 1);
+  const int64_t eff_bn = d.block_n * (p.fuse == 2 ? 2 : 1);
+  if (eff_bm <= 128) {
     p.cta_m = 128;
     p.ctas_per_tile = 1;
-    if (d.block_n <= 64) { p.kernel_tile = kTile128x64; p.cta_n = 64; }
-    else if (d.block_n <= 128) { p.kernel_tile = kTile128x128; p.cta_n = 128; }
+    if (eff_bn <= 64) { p.kernel_tile = kTile128x64; p.cta_n = 64; }
+    else if (eff_bn <= 128) { p.kernel_tile = kTile128x128; p.cta_n = 128; }
     else { p.kernel_tile = kTile128x256; p.cta_n = 256; }
   } else {
     p.cta_m = 256;
     p.ctas_per_tile = 2;
-    if (d.block_n <= 128) { p.kernel_tile = kTile256x128; p.cta_n = 128; }
+    if (eff_bn <= 128) { p.kernel_tile = kTile256x128; p.cta_n = 128; }
     else { p.kernel_tile = kTile256x256; p.cta_n = 256; }
   }
   // The ring is as deep as shared memory allows and never shallower than
@@ -345,7 +361,7 @@ extern "C" tbStatus tb_matmul_plan_create(const tb_matmul_desc* desc, int device
     else p.workspace_bytes = p.partial_bytes;
   }
   // Resident program slots: one per SM, or one per SM pair for CTA pairs.
-  const int64_t want = d.persistent ? p.resident_programs : total;
+  const int64_t want = d.persistent ? std::min<int64_t>(p.resident_programs, p.work_items) : p.work_items;
   const int64_t slots = std::max<int64_t>(1, num_sms / p.ctas_per_tile);
   p.grid = p.ctas_per_tile * std::max<int64_t>(1, std::min<int64_t>(want, slots));
 
@@ -419,6 +435,9 @@ extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* bu
   o << "\"kernel\": \"" << kernel_names[plan->kernel_tile] << "\", ";
   o << "\"cta_tile\": [" << plan->cta_m << ", " << plan->cta_n << ", " << plan->kb << "], ";
   o << "\"ctas_per_tile\": " << plan->ctas_per_tile << ", ";
+  o << "\"fused_program_pairs\": \"" << (plan->fuse == 1 ? "vertical" : plan->fuse == 2 ? "horizontal" : "none")
+    << "\", ";
+  o << "\"work_items\": " << plan->work_items << ", ";
   o << "\"stages\": " << plan->stages << ", ";
   o << "\"smem_bytes\": " << plan->smem_bytes << ", ";
   o << "\"tmem_cols\": " << plan->tmem_cols << ", ";

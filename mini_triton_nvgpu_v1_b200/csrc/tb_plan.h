@@ -47,6 +47,12 @@ struct tb_matmul_plan {
 
   // --- this build's launch facts ---
   int32_t kernel_tile;         // TbKernelTile
+  // Program pairing: two consecutive program ids whose tiles are adjacent in
+  // the reference's launch order run as one hardware work item (same
+  // programs, same results): 1 = vertical pair (grouped order, even group),
+  // 2 = horizontal pair (row-major / persistent order), 0 = none.
+  int32_t fuse;
+  int64_t work_items;          // total_programs / (fuse ? 2 : 1)
   int32_t cta_m, cta_n;        // hardware tile (cta_m = 256: a CTA pair)
   int32_t ctas_per_tile;       // 1 or 2
   int32_t stages;              // shared-memory ring depth

@@ -91,6 +91,12 @@ CASES = [
     ("splitk_parallel_ragged_tma", (1000, 600, 2048), dict(block_m=256, block_n=256, block_k=64,
                                                            split_k=5, exact_tile=False,
                                                            reduction_mode="split_k_parallel"), "uniform", 16),
+    ("fused_vertical_ragged", (1000, 600, 256), dict(block_m=128, block_n=128, block_k=64, group_m=4,
+                                                     exact_tile=False), "uniform", 17),
+    ("fused_horizontal_ragged", (300, 1000, 200), dict(block_m=128, block_n=128, block_k=64, group_m=1,
+                                                       exact_tile=False), "uniform", 18),
+    ("fused_horizontal_persistent", (512, 1024, 256), dict(block_m=128, block_n=64, block_k=64,
+                                                           persistent=True, num_ctas=7), "uniform", 19),
     ("splitk_parallel_512x512x4096_s8", (512, 512, 4096), dict(block_m=128, block_n=128, block_k=64,
                                                                split_k=8,
                                                                reduction_mode="split_k_parallel"),

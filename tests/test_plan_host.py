@@ -167,6 +167,25 @@ def test_num_ctas_clamped_to_sms_and_programs():
     assert plan(192, 128, 32, 64, 64, 32, persistent=True, num_ctas=100).info["num_ctas"] == 6
 
 
+def test_program_pairing():
+    """Two consecutive programs with adjacent tiles share a hardware tile when
+    every pair in the launch order is aligned; the program set is unchanged."""
+    p = plan(4096, 4096, 4096, 128, 128, 64)                     # grouped, group 8
+    assert p.info["fused_program_pairs"] == "vertical" and p.info["kernel"] == "tb_gemm_sm100_pair_256x128"
+    assert p.info["work_items"] * 2 == p.total_programs
+    for w in range(0, p.info["work_items"], 37):
+        a, b = p.program_work(2 * w), p.program_work(2 * w + 1)
+        assert a[0] % 2 == 0 and b[0] == a[0] + 1 and b[1] == a[1]          # vertical neighbours
+    q = plan(192, 128, 32, 64, 64, 32, persistent=True, num_ctas=2)          # row-major persistent
+    assert q.info["fused_program_pairs"] == "horizontal"
+    for w in range(q.info["work_items"]):
+        a, b = q.program_work(2 * w), q.program_work(2 * w + 1)
+        assert a[1] % 2 == 0 and b[1] == a[1] + 1 and b[0] == a[0]
+    assert plan(192, 128, 32, 64, 64, 32, group_m=2).info["fused_program_pairs"] == "none"   # 3 tile rows
+    assert plan(512, 512, 8192, 128, 256, 64, split_k=4).info["fused_program_pairs"] == "none"
+    assert plan(8192, 8192, 8192, 256, 256, 64).info["fused_program_pairs"] == "none"
+
+
 def test_workspace_bytes():
     assert plan(512, 512, 65536, 128, 256, 64, split_k=16).workspace_bytes == 16 * 512 * 512 * 4
     assert plan(512, 512, 65536, 128, 256, 64, split_k=16,
@@ -177,7 +196,7 @@ def test_workspace_bytes():
 def test_hardware_tile_selection():
     assert plan(64, 64, 32, 64, 64, 32).info["kernel"] == "tb_gemm_sm100_128x64"
     assert plan(96, 80, 32, 128, 128, 64, exact_tile=False).info["kernel"] == "tb_gemm_sm100_128x128"
-    assert plan(8192, 8192, 8192, 128, 256, 64).info["kernel"] == "tb_gemm_sm100_128x256"
+    assert plan(8192, 8192, 8192, 128, 256, 64, group_m=3).info["kernel"] == "tb_gemm_sm100_128x256"
     info = plan(8192, 8192, 8192, 256, 256, 64).info
     assert info["kernel"] == "tb_gemm_sm100_pair_256x256" and info["ctas_per_tile"] == 2
     assert info["grid"] == 148 and info["tmem_cols"] == 512 and info["smem_bytes"] <= 232448
