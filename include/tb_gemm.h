@@ -62,7 +62,8 @@ typedef enum tbReductionMode {
 
 /* Knobs of one tb.matmul. Field names follow the reference attributes. */
 typedef struct tb_matmul_desc {
-  int64_t m, n, k;                 /* A: m×k, B: k×n, C: m×n (static shapes) */
+  int64_t m, n, k;                 /* A: m×k, B: k×n, C: m×n; TB_DIM_DYNAMIC
+                                      (dynamic plans only) leaves one open */
   int64_t block_m, block_n, block_k; /* TBOps.td:42-44 */
   int64_t group_m;                 /* TBOps.td:45, default 8 */
   int32_t exact_tile;              /* TBOps.td:46, default 1 */
@@ -92,6 +93,10 @@ typedef struct tb_matmul_desc {
    * b_col_major: B is k × n column-major, ldb >= k (B^T row-major). */
   int32_t a_col_major, b_col_major;
 } tb_matmul_desc;
+
+/* An open ("?") problem dim, for tb_matmul_plan_create_dynamic; the value
+ * MLIR gives a dynamic memref dim (ShapedType::kDynamic = INT64_MIN). */
+#define TB_DIM_DYNAMIC INT64_MIN
 
 typedef enum tbActivation {
   TB_ACT_NONE = 0,
@@ -222,6 +227,32 @@ tbStatus tb_matmul_run_epilogue(const tb_matmul_plan* plan, const void* A,
                                 void* C, int64_t ldc, const float* bias,
                                 void* workspace, size_t workspace_bytes,
                                 void* stream);
+
+/* ---- Dynamic shapes ----
+ * The reference accepts static memref shapes only (deriveSourceKernelConfig,
+ * lib/Analysis/KernelConfig.cpp:98-103 — tb_matmul_plan_create rejects a
+ * TB_DIM_DYNAMIC dim with the same message). A dynamic plan validates its
+ * knobs once; each run names m, n and k, which must equal the desc's static
+ * dims where those are given. The concrete per-shape plan (mapping, hardware
+ * tile, grid, workspace) is derived on a shape's first run and cached inside
+ * the plan (thread-safe; bounded to 256 shapes). Static-plan entry points
+ * (tb_matmul_run, tb_matmul_run_no_alloc, tb_matmul_program_work,
+ * tb_matmul_run_kshard_peer) reject a dynamic plan; tb_matmul_workspace_bytes
+ * returns 0 for it. No counterpart in the reference. */
+tbStatus tb_matmul_plan_create_dynamic(const tb_matmul_desc* desc, int device,
+                                       tb_matmul_plan** plan);
+/* Workspace bytes of one shape of a dynamic plan (monotone in m, n and k). */
+tbStatus tb_matmul_workspace_bytes_dynamic(const tb_matmul_plan* plan, int64_t m,
+                                           int64_t n, int64_t k, size_t* bytes);
+/* tb_matmul_run_epilogue for shape m×n×k (bias: NULL unless desc.bias). */
+tbStatus tb_matmul_run_dynamic(const tb_matmul_plan* plan, int64_t m, int64_t n,
+                               int64_t k, const void* A, int64_t lda, const void* B,
+                               int64_t ldb, void* C, int64_t ldc, const float* bias,
+                               void* workspace, size_t workspace_bytes, void* stream);
+/* A new static plan equal to the dynamic plan's concrete plan for m×n×k
+ * (destroy it with tb_matmul_plan_destroy). */
+tbStatus tb_matmul_plan_for_shape(const tb_matmul_plan* plan, int64_t m, int64_t n,
+                                  int64_t k, tb_matmul_plan** shape_plan);
 
 /* One-call convenience: desc → plan → run → destroy. */
 tbStatus tb_matmul(const tb_matmul_desc* desc, const void* A, int64_t lda,

@@ -45,7 +45,7 @@ class _LazyLib:
 
 _lib = _LazyLib()
 
-__all__ = ["KernelConfig", "MatmulPlan", "TBError", "matmul", "plan_for", "version", "lib"]
+__all__ = ["KernelConfig", "MatmulPlan", "DynamicMatmulPlan", "TBError", "matmul", "plan_for", "version", "lib"]
 
 _REDUCTION = {None: TB_REDUCTION_UNSET, "": TB_REDUCTION_UNSET,
               "split_k_serial": TB_REDUCTION_SPLIT_K_SERIAL,
@@ -107,7 +107,8 @@ class KernelConfig:
     def to_desc(self) -> _capi.tb_matmul_desc:
         d = _capi.tb_matmul_desc()
         _check(_lib.tb_matmul_desc_init(C.byref(d)))
-        d.m, d.n, d.k = self.m, self.n, self.k
+        # None leaves a dim open ("?"): only dynamic plans accept it
+        d.m, d.n, d.k = (_capi.TB_DIM_DYNAMIC if x is None else x for x in (self.m, self.n, self.k))
         d.block_m, d.block_n, d.block_k = self.block_m, self.block_n, self.block_k
         d.group_m = self.group_m
         d.exact_tile = 1 if self.exact_tile else 0
@@ -212,7 +213,75 @@ class MatmulPlan:
                      Cm.stride(0), ws_ptr, ws_bytes, s.cuda_stream, bias_ptr)
 
 
-def _check_tensors(cfg: KernelConfig, A, B, Cm) -> None:
+class DynamicMatmulPlan:
+    """A plan whose problem dims may be left open (``None`` in the
+    KernelConfig, ``memref<?x…>`` in the reference spelling, which the
+    reference rejects). Knobs are validated once here; each ``run`` takes its
+    shape from the tensors, and the library derives and caches the concrete
+    plan of each shape (C ABI ``tb_matmul_plan_create_dynamic``)."""
+
+    def __init__(self, cfg: KernelConfig, device: Optional[int] = None):
+        self.cfg = cfg
+        self._h = C.c_void_p()
+        desc = cfg.to_desc()
+        _check(_lib.tb_matmul_plan_create_dynamic(C.byref(desc), -1 if device is None else int(device),
+                                                  C.byref(self._h)))
+        self.device = device
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        lib_ = _lib_handle
+        if h is not None and h.value and lib_ is not None:
+            lib_.tb_matmul_plan_destroy(h)
+            self._h = C.c_void_p()
+
+    @property
+    def info(self) -> dict:
+        return MatmulPlan._describe(self)
+
+    def workspace_bytes(self, m: int, n: int, k: int) -> int:
+        out = C.c_size_t(0)
+        _check(_lib.tb_matmul_workspace_bytes_dynamic(self._h, m, n, k, C.byref(out)))
+        return int(out.value)
+
+    def shape_info(self, m: int, n: int, k: int) -> dict:
+        """Plan facts of the concrete plan for m×n×k."""
+        h = C.c_void_p()
+        _check(_lib.tb_matmul_plan_for_shape(self._h, m, n, k, C.byref(h)))
+        try:
+            need = C.c_size_t(0)
+            _lib.tb_matmul_plan_describe(h, None, 0, C.byref(need))
+            buf = C.create_string_buffer(need.value)
+            _check(_lib.tb_matmul_plan_describe(h, buf, need.value, C.byref(need)))
+            return json.loads(buf.value.decode())
+        finally:
+            _lib.tb_matmul_plan_destroy(h)
+
+    def run(self, A, B, Cm, workspace=None, stream=None, bias=None) -> None:
+        """C ← beta·C + A·B in place for the tensors' own m, n, k."""
+        import torch
+        m, k = A.shape
+        n = B.shape[1]
+        _check_tensors(self.cfg, A, B, Cm, shape=(m, n, k))
+        ws_ptr, ws_bytes = 0, 0
+        need = self.workspace_bytes(m, n, k)
+        if need:
+            if workspace is None:
+                workspace = torch.empty(need, dtype=torch.uint8, device=Cm.device)
+            ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+        if bias is not None and (bias.dtype != torch.float32 or bias.numel() != n
+                                 or not bias.is_contiguous() or not bias.is_cuda):
+            raise TBError(_capi.TB_ERR_INVALID_ARGUMENT, "bias must be a contiguous f32 CUDA vector of n")
+        s = stream if stream is not None else torch.cuda.current_stream(Cm.device)
+        lda = A.stride(1) if self.cfg.a_col_major else A.stride(0)
+        ldb = B.stride(1) if self.cfg.b_col_major else B.stride(0)
+        _check(_lib.tb_matmul_run_dynamic(self._h, m, n, k, A.data_ptr(), lda, B.data_ptr(), ldb,
+                                          Cm.data_ptr(), Cm.stride(0),
+                                          None if bias is None else bias.data_ptr(),
+                                          ws_ptr or None, ws_bytes, s.cuda_stream or None))
+
+
+def _check_tensors(cfg: KernelConfig, A, B, Cm, shape=None) -> None:
     import torch
     if A.dtype != torch.float16 or B.dtype != torch.float16:
         raise TBError(_capi.TB_ERR_INVALID_ARGUMENT,
@@ -228,8 +297,8 @@ def _check_tensors(cfg: KernelConfig, A, B, Cm) -> None:
         if t.stride(0 if col else 1) != 1:
             raise TBError(_capi.TB_ERR_UNSUPPORTED,
                           f"{name} must have a unit stride along its {'rows' if col else 'columns'}")
-    if tuple(A.shape) != (cfg.m, cfg.k) or tuple(B.shape) != (cfg.k, cfg.n) or \
-            tuple(Cm.shape) != (cfg.m, cfg.n):
+    m, n, k = shape if shape is not None else (cfg.m, cfg.n, cfg.k)
+    if tuple(A.shape) != (m, k) or tuple(B.shape) != (k, n) or tuple(Cm.shape) != (m, n):
         raise TBError(_capi.TB_ERR_INVALID_ARGUMENT, "operand shapes disagree with the plan")
 
 

@@ -60,6 +60,9 @@ class tb_matmul_desc(C.Structure):
     ]
 
 
+TB_DIM_DYNAMIC = -(1 << 63)  # INT64_MIN, MLIR's ShapedType::kDynamic
+
+
 class tb_program_work(C.Structure):
     _fields_ = [
         ("tile_m", C.c_int64), ("tile_n", C.c_int64), ("split_part", C.c_int64),
@@ -86,6 +89,14 @@ PROTOTYPES = {
     "tb_matmul_run_epilogue": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
                                          C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_size_t,
                                          C.c_void_p]),
+    "tb_matmul_plan_create_dynamic": (C.c_int, [C.POINTER(tb_matmul_desc), C.c_int, C.POINTER(C.c_void_p)]),
+    "tb_matmul_workspace_bytes_dynamic": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
+                                                    C.POINTER(C.c_size_t)]),
+    "tb_matmul_run_dynamic": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_void_p, C.c_int64,
+                                        C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p,
+                                        C.c_void_p, C.c_size_t, C.c_void_p]),
+    "tb_matmul_plan_for_shape": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
+                                           C.POINTER(C.c_void_p)]),
     "tb_matmul": (C.c_int, [C.POINTER(tb_matmul_desc), C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
                             C.c_void_p, C.c_int64, C.c_void_p, C.c_size_t, C.c_void_p]),
     "tb_peer_comm_create": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,

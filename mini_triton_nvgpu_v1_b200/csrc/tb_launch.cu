@@ -991,6 +991,9 @@ tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda, const
 tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, const void* B,
                       int64_t ldb, void* Cp, int64_t ldc, const float* bias, void* workspace,
                       size_t workspace_bytes, void* stream_v) {
+  if (plan->dynamic)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "this plan has dynamic dims: run it with tb_matmul_run_dynamic");
   const tb_matmul_desc& d = plan->desc;
   if (d.bias && !bias)
     return tb_fail(TB_ERR_INVALID_ARGUMENT,
@@ -1219,6 +1222,9 @@ extern "C" tbStatus tb_matmul_run_no_alloc(const tb_matmul_plan* plan, const voi
                                            void* stream) {
   tb_clear_error();
   if (!plan) return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan must not be NULL");
+  if (plan->dynamic)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "this plan has dynamic dims: run it with tb_matmul_run_dynamic");
   const size_t need = plan->workspace_bytes;
   if (need > kNoAllocScratchBytes)
     return tb_fail(TB_ERR_WORKSPACE,

@@ -277,6 +277,8 @@ extern "C" tbStatus tb_matmul_run_kshard_peer(const tb_matmul_plan* plan, tb_pee
   tb_clear_error();
   if (!plan || !c || !c->connected)
     return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan and a connected comm are required");
+  if (plan->dynamic)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "K-sharded runs take a plan with static dims");
   if (plan->desc.m != c->rows_per_rank * c->world || plan->desc.n != c->n)
     return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan m must be world * rows_per_rank and n the comm's n");
   if (plan->epilogue == kEpiWorkspace)

@@ -113,6 +113,10 @@ static tbStatus validate_kernel_config(const tb_matmul_desc& d) {
       (d.c_dtype != TB_F32 && d.c_dtype != TB_F16))
     return tb_fail(TB_ERR_INVALID_ARGUMENT,
                    "stage1 currently supports fp16 x fp16 -> fp32 matmul kernels");
+  if (d.m == TB_DIM_DYNAMIC || d.n == TB_DIM_DYNAMIC || d.k == TB_DIM_DYNAMIC)  // KernelConfig.cpp:98-103
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "stage1 supported envelope currently requires static rank-2 memrefs to "
+                   "derive problem shape coverage");
   if (d.m <= 0 || d.n <= 0 || d.k <= 0)
     return tb_fail(TB_ERR_INVALID_ARGUMENT, "problem M/N/K must be positive");
   if (d.block_m <= 0 || d.block_n <= 0 || d.block_k <= 0)
@@ -155,8 +159,21 @@ extern "C" tbStatus tb_matmul_plan_create(const tb_matmul_desc* desc, int device
                                       cudaGetErrorString(e));
     num_sms = n;
   }
+  tb_matmul_plan* heap = new (std::nothrow) tb_matmul_plan();
+  if (!heap) return tb_fail(TB_ERR_INVALID_ARGUMENT, "out of host memory");
+  st = tb_plan_build(d, device, num_sms, heap);
+  if (st != TB_OK) {
+    delete heap;
+    return st;
+  }
+  *out = heap;
+  return TB_OK;
+}
 
-  tb_matmul_plan p;
+tbStatus tb_plan_build(const tb_matmul_desc& d, int device, int num_sms, tb_matmul_plan* out) {
+  tbStatus st = validate_kernel_config(d);
+  if (st != TB_OK) return st;
+  tb_matmul_plan& p = *out;
   p.desc = d;
   p.device = device;
   p.num_sms = num_sms;
@@ -365,9 +382,6 @@ extern "C" tbStatus tb_matmul_plan_create(const tb_matmul_desc* desc, int device
   const int64_t slots = std::max<int64_t>(1, num_sms / p.ctas_per_tile);
   p.grid = p.ctas_per_tile * std::max<int64_t>(1, std::min<int64_t>(want, slots));
 
-  tb_matmul_plan* heap = new (std::nothrow) tb_matmul_plan(p);
-  if (!heap) return tb_fail(TB_ERR_INVALID_ARGUMENT, "out of host memory");
-  *out = heap;
   return TB_OK;
 }
 
@@ -377,12 +391,15 @@ extern "C" tbStatus tb_matmul_plan_destroy(tb_matmul_plan* plan) {
 }
 
 extern "C" size_t tb_matmul_workspace_bytes(const tb_matmul_plan* plan) {
-  return plan ? plan->workspace_bytes : 0;
+  return plan && !plan->dynamic ? plan->workspace_bytes : 0;
 }
 
 extern "C" tbStatus tb_matmul_program_work(const tb_matmul_plan* plan, int64_t pid,
                                            tb_program_work* w) {
   if (!plan || !w) return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan and work must not be NULL");
+  if (plan->dynamic)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT,
+                   "program work of a dynamic plan: take tb_matmul_plan_for_shape first");
   if (pid < 0 || pid >= plan->map.total_programs)
     return tb_fail(TB_ERR_INVALID_ARGUMENT, "program id out of range");
   const tb::Work x = tb::program_work(plan->map, (int32_t)pid);
@@ -397,6 +414,14 @@ extern "C" tbStatus tb_matmul_program_work(const tb_matmul_plan* plan, int64_t p
 extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* buf,
                                             size_t len, size_t* needed) {
   if (!plan) return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan must not be NULL");
+  if (plan->dynamic) {
+    const std::string s = tb_describe_dynamic(plan);
+    if (needed) *needed = s.size() + 1;
+    if (!buf || len < s.size() + 1)
+      return tb_fail(TB_ERR_INVALID_ARGUMENT, "describe buffer too small");
+    std::memcpy(buf, s.c_str(), s.size() + 1);
+    return TB_OK;
+  }
   const tb_matmul_desc& d = plan->desc;
   const char* kernel_names[] = {"tb_gemm_sm100_128x64", "tb_gemm_sm100_128x128",
                                 "tb_gemm_sm100_128x256", "tb_gemm_sm100_pair_256x128",

@@ -4,6 +4,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <memory>
 #include <string>
 
 #include "../../include/tb_gemm.h"
@@ -25,8 +26,15 @@ enum TbEpilogue : int32_t {
   kEpiAtomic = 2,     // C += acc atomically (split_k_parallel)
 };
 
+struct TbShapeCache;  // tb_dynamic.cpp
+
 struct tb_matmul_plan {
   tb_matmul_desc desc;
+  // Dynamic plan: desc.m/n/k equal to TB_DIM_DYNAMIC are left open ("?" dims) and every run
+  // names its shape; the concrete per-shape plans live in `shapes`. All the
+  // facts below are then those of a probe shape and are not used for launch.
+  bool dynamic = false;
+  std::shared_ptr<TbShapeCache> shapes;
   int device;
   int num_sms;
 
@@ -77,6 +85,12 @@ tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda,
 size_t tb_kernel_smem_bytes(int32_t kernel_tile, int32_t stages);
 int32_t tb_kernel_max_stages(int32_t kernel_tile);
 int32_t tb_kernel_kb(int32_t kernel_tile);
+
+// Derives a concrete plan for `d` (validated) into *out; tb_plan.cpp.
+tbStatus tb_plan_build(const tb_matmul_desc& d, int device, int num_sms, tb_matmul_plan* out);
+
+// JSON facts of a dynamic plan; tb_dynamic.cpp.
+std::string tb_describe_dynamic(const tb_matmul_plan* plan);
 
 // Thread-local error message helpers (tb_plan.cpp).
 tbStatus tb_fail(tbStatus code, const std::string& msg);

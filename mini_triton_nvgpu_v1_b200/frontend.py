@@ -35,7 +35,7 @@ import sys
 from dataclasses import dataclass
 from typing import Optional
 
-from . import KernelConfig, MatmulPlan, TBError
+from . import DynamicMatmulPlan, KernelConfig, MatmulPlan, TBError
 from . import _capi
 
 _ERR = _capi.TB_ERR_INVALID_ARGUMENT
@@ -128,9 +128,11 @@ def _op_error(msg: str) -> TBError:
     return TBError(_ERR, f"'tb.matmul' op {msg}")
 
 
-def parse_module(text: str, allow_f16_c: bool = False) -> list[MatmulSpec]:
+def parse_module(text: str, allow_f16_c: bool = False, allow_dynamic: bool = False) -> list[MatmulSpec]:
     """Every tb.matmul of `text` as a MatmulSpec (knobs validated by the
-    reference's rules when a plan is made)."""
+    reference's rules when a plan is made). `allow_dynamic` accepts `?` dims
+    (the reference rejects them): they stay None in the config and need a
+    DynamicMatmulPlan."""
     text = _strip_comments(text)
     mod_attrs: dict = {}
     m = re.search(r"module\s+attributes\s*\{", text)
@@ -188,7 +190,7 @@ def parse_module(text: str, allow_f16_c: bool = False) -> list[MatmulSpec]:
                 return x is not None and y is not None and x != y
             if mismatch(ad[1], bd[0]) or mismatch(ad[0], cd[0]) or mismatch(bd[1], cd[1]):
                 raise _op_error("expected A:[M,K], B:[K,N], C:[M,N] operand shapes")
-            if None in ad + bd + cd:
+            if None in ad + bd + cd and not allow_dynamic:
                 raise TBError(_ERR, "stage1 supported envelope currently requires static "
                                     "rank-2 memrefs to derive problem shape coverage")
 
@@ -207,8 +209,10 @@ def parse_module(text: str, allow_f16_c: bool = False) -> list[MatmulSpec]:
                 raise _op_error("group_m must be positive")
             exact = attrs.get("exact_tile", ("bool", True))[1]
             red = opt("tb.reduction-mode", "string", "")
+            def pick(x, y):
+                return x if x is not None else y
             cfg = KernelConfig(
-                m=ad[0], n=bd[1], k=ad[1], block_m=bm, block_n=bn, block_k=bk, group_m=gm,
+                m=pick(ad[0], cd[0]), n=pick(bd[1], cd[1]), k=pick(ad[1], bd[0]), block_m=bm, block_n=bn, block_k=bk, group_m=gm,
                 exact_tile=bool(exact), num_warps=req_i64("tb.num-warps"),
                 num_stages=req_i64("tb.requested-stages"), split_k=opt("tb.split-k", "int", 1),
                 reduction_mode=red or None, persistent=opt("tb.persistent", "bool", False),
@@ -219,6 +223,13 @@ def parse_module(text: str, allow_f16_c: bool = False) -> list[MatmulSpec]:
     if not specs:
         raise TBError(_ERR, "no tb.matmul op found")
     return specs
+
+
+class _ShapeView:
+    """plan_facts input made from a describe dict."""
+
+    def __init__(self, info: dict):
+        self.info = info
 
 
 def plan_facts(plan: MatmulPlan) -> str:
@@ -257,17 +268,34 @@ def checksum_line(C) -> str:
             f"checksum={float(flat.double().sum() if hasattr(flat, 'double') else flat.sum()):.6g}")
 
 
-def run_spec(spec: MatmulSpec, seed: int = 0, device: int = 0):
-    """Runs one tb.matmul on seeded U[-1,1] inputs (C_in = 0) and returns C."""
+def dynamic_facts(plan: DynamicMatmulPlan) -> str:
+    """The shape-independent facts of a dynamic plan, `?` for open dims."""
+    i = plan.info
+    dims = "x".join("?" if d is None else str(d) for d in i["problem"])
+    return (f'tb.dynamic_plan = {{problem = "{dims}", tile = {i["tile"]}, num_warps = {i["num_warps"]}, '
+            f'warp_grid = array<i64: {i["warp_grid"][0]}, {i["warp_grid"][1]}>, '
+            f'split_k = {i["split_k"]}, reduction_kind = "{i["reduction_kind"]}", '
+            f'persistent = {str(i["persistent"]).lower()}}}')
+
+
+def run_spec(spec: MatmulSpec, seed: int = 0, device: int = 0, shape=None):
+    """Runs one tb.matmul on seeded U[-1,1] inputs (C_in = 0) and returns C.
+    `shape` (m, n, k) fills a dynamic spec's open dims (through one
+    DynamicMatmulPlan)."""
     import torch
     from . import matmul
     cfg = spec.config
     dev = torch.device("cuda", device)
+    m, n, k = shape if shape is not None else (cfg.m, cfg.n, cfg.k)
     g = torch.Generator(device=dev).manual_seed(seed)
-    A = (torch.rand(cfg.m, cfg.k, device=dev, generator=g) * 2 - 1).half()
-    B = (torch.rand(cfg.k, cfg.n, device=dev, generator=g) * 2 - 1).half()
-    C = torch.zeros(cfg.m, cfg.n, device=dev,
+    A = (torch.rand(m, k, device=dev, generator=g) * 2 - 1).half()
+    B = (torch.rand(k, n, device=dev, generator=g) * 2 - 1).half()
+    C = torch.zeros(m, n, device=dev,
                     dtype=torch.float16 if cfg.c_dtype == "f16" else torch.float32)
+    if None in (cfg.m, cfg.n, cfg.k):
+        DynamicMatmulPlan(cfg, device).run(A, B, C)
+        torch.cuda.synchronize(dev)
+        return A, B, C
     matmul(A, B, C, block_m=cfg.block_m, block_n=cfg.block_n, block_k=cfg.block_k,
            group_m=cfg.group_m, exact_tile=cfg.exact_tile, num_warps=cfg.num_warps,
            num_stages=cfg.num_stages, split_k=cfg.split_k, reduction_mode=cfg.reduction_mode,
@@ -282,12 +310,29 @@ def main(argv: Optional[list] = None) -> int:
     ap.add_argument("--run", action="store_true", help="execute on cuda:0 and print a checksum line")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--allow-f16-c", action="store_true")
+    ap.add_argument("--dynamic", action="store_true",
+                    help="accept `?` dims (one plan for every shape)")
+    ap.add_argument("--shape", default=None, help="MxNxK for --run of a dynamic op")
     args = ap.parse_args(argv)
     try:
-        specs = parse_module(open(args.file).read(), allow_f16_c=args.allow_f16_c)
+        specs = parse_module(open(args.file).read(), allow_f16_c=args.allow_f16_c,
+                             allow_dynamic=args.dynamic)
+        shape = tuple(int(x) for x in args.shape.split("x")) if args.shape else None
         for spec in specs:
-            plan = MatmulPlan(spec.config, None)
             print(f"// @{spec.func}: tb.matmul {spec.a_type}, {spec.b_type}, {spec.c_type}")
+            cfg = spec.config
+            if None in (cfg.m, cfg.n, cfg.k):
+                dplan = DynamicMatmulPlan(cfg, None)
+                print(dynamic_facts(dplan))
+                if shape is not None:
+                    print(plan_facts(_ShapeView(dplan.shape_info(*shape))))
+                if args.run:
+                    if shape is None:
+                        raise TBError(_ERR, "--run of an op with `?` dims needs --shape MxNxK")
+                    _, _, C = run_spec(spec, args.seed, shape=shape)
+                    print(checksum_line(C))
+                continue
+            plan = MatmulPlan(cfg, None)
             print(plan_facts(plan))
             if args.run:
                 _, _, C = run_spec(spec, args.seed)

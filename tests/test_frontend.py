@@ -135,3 +135,38 @@ def test_run_from_module_text_matches_oracle(cuda, name):
     assert float(np.abs(C.cpu().numpy() - ref).max()) <= oracle.tolerance(k)
     line = fe.checksum_line(C)
     assert line.startswith("c00=") and "checksum=" in line
+
+
+DYN_TEXT = """module attributes {"tb.num-warps" = 4 : i64, "tb.requested-stages" = 2 : i64} {
+  func.func @k(%A: memref<?x256xf16>, %B: memref<256x?xf16>, %C: memref<?x?xf32>) {
+    tb.matmul %A, %B, %C {block_m = 128 : i64, block_n = 128 : i64, block_k = 64 : i64, exact_tile = false}
+      : memref<?x256xf16>, memref<256x?xf16>, memref<?x?xf32>
+    return
+  }
+}
+"""
+
+
+def test_dynamic_dims_are_opt_in(tmp_path, capsys):
+    with pytest.raises(tb.TBError, match="requires static rank-2 memrefs"):
+        fe.parse_module(DYN_TEXT)
+    (spec,) = fe.parse_module(DYN_TEXT, allow_dynamic=True)
+    assert (spec.config.m, spec.config.n, spec.config.k) == (None, None, 256)
+    p = tmp_path / "dyn.mlir"
+    p.write_text(DYN_TEXT)
+    assert fe.main([str(p)]) == 1
+    assert fe.main([str(p), "--dynamic", "--shape", "1000x512x256"]) == 0
+    out = capsys.readouterr().out
+    assert 'problem = "?x?x256"' in out and "total_programs = 32" in out
+    # the open dims must agree with the static K
+    assert fe.main([str(p), "--dynamic", "--shape", "1000x512x128"]) == 1
+
+
+@pytest.mark.gpu
+def test_dynamic_module_runs_at_two_shapes(cuda):
+    import oracle
+    (spec,) = fe.parse_module(DYN_TEXT, allow_dynamic=True)
+    for shape in [(1000, 512, 256), (96, 80, 256)]:
+        A, B, C = fe.run_spec(spec, seed=4, shape=shape)
+        ref = oracle.matmul_ref(A.cpu().numpy(), B.cpu().numpy())
+        assert float(np.abs(C.cpu().numpy() - ref).max()) <= oracle.tolerance(256)
