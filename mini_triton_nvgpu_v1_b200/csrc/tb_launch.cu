@@ -32,6 +32,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstring>
 #include <cstdio>
@@ -78,9 +79,19 @@ constexpr uint32_t kSiteProducer = 1, kSiteMma = 2, kSiteEpilogue = 3, kSiteDrai
 // barrier handshake; 8 MMAs per stage amortise it: measured −15 % time for
 // 128×64 and −9 % for the 256×128 pair at 8192³; 128×128 is L2-feed bound
 // and gains nothing).
+// BN = 512 (CTA pair only, for 256 < block_n <= 512): two N = 256 MMAs per
+// K step share each A tile (25 % less L2→SM operand traffic per FLOP than
+// 256 × 256); its accumulator fills TMEM, so there is one accumulator and the
+// epilogue does not overlap the next tile's MMAs.
 template <int BN, int G>
 struct Cfg {
   static constexpr int kBnCta = BN / G;                  // B columns per CTA
+  static constexpr int kMmaN = BN > 256 ? 256 : BN;      // N of one tcgen05.mma
+  static constexpr int kMmaPerK = BN / kMmaN;            // MMAs per K step (1 or 2)
+  static constexpr int kAccs = 2 * BN <= 512 ? 2 : 1;    // TMEM accumulators
+  // B bytes per CTA feeding one MMA of a K step (the second MMA's B starts
+  // this far into the stage: MN-major box 2, or K-major row 128).
+  static constexpr uint32_t kBHalf = (uint32_t)(kBnCta / kMmaPerK) * 64 * 2;
   static constexpr int kKB = kBnCta <= 64 ? 128 : 64;
   static constexpr uint32_t kABytes = kCtaM * kKB * 2;   // KB/64 K-major [128 × 64] sub-tiles
   static constexpr uint32_t kASub = kCtaM * 64 * 2;      // one K-major A sub-tile
@@ -99,9 +110,10 @@ struct Cfg {
   static constexpr int kCap = 8;
 #endif
   static constexpr int kStages = kRawStages > kCap ? kCap : kRawStages;
-  static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators of BN f32 columns
+  static constexpr uint32_t kTmemCols = kAccs * BN;  // kAccs accumulators of BN f32 columns
   static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + kEpiBytes + 512;
   static_assert(kBnCta % 64 == 0, "B columns per CTA must be whole 64-column boxes");
+  static_assert(kMmaPerK == 1 || (G == 2 && kKB == 64), "BN = 512 is a CTA-pair tile");
   static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512, "TMEM columns");
 };
 
@@ -392,7 +404,20 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < Cf::kKB / 64; ++j)
                 tma_load_2d_pair(dA + j * Cf::kASub, &tmA, fb, kx + 64 * j, am);
             }
-            if (p.b_kmaj) {  // KB/64 [kBnCta n × 64 k] sub-tiles
+            if constexpr (Cf::kMmaPerK == 2) {
+              // Per MMA h, this CTA holds columns [256·h + 128·rank, +128):
+              // TMEM column c of the pair's accumulator is tile column c.
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int32_t nh = e.n0 + 256 * h + (int32_t)rank * 128;
+                if (p.b_kmaj) {  // one [128 n × 64 k] box
+                  tma_load_2d_pair(dB + h * Cf::kBHalf, &tmB, fb, kx, nh);
+                } else {         // two [64 k × 64 n] boxes
+                  tma_load_2d_pair(dB + h * Cf::kBHalf, &tmB, fb, nh, kx);
+                  tma_load_2d_pair(dB + h * Cf::kBHalf + Cf::kBoxBytes, &tmB, fb, nh + 64, kx);
+                }
+              }
+            } else if (p.b_kmaj) {  // KB/64 [kBnCta n × 64 k] sub-tiles
 #pragma unroll
               for (int j = 0; j < Cf::kKB / 64; ++j)
                 tma_load_2d_pair(dB + j * Cf::kBSub, &tmB, fb, kx + 64 * j, bn);
@@ -455,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Leader CTA only. Whole warp runs the loop; descriptors are computed
     // warp-uniformly and one elected lane issues tcgen05.mma / commit.
     if (leader) {
-      const uint32_t idesc = idesc_f16_f32(kCtaM * G, BN, p.a_mn ? 1 : 0, p.b_kmaj ? 0 : 1);
+      const uint32_t idesc = idesc_f16_f32(kCtaM * G, Cf::kMmaN, p.a_mn ? 1 : 0, p.b_kmaj ? 0 : 1);
       // Per-operand layout in shared memory (all 128-byte swizzled):
       //   K-major: sub-tiles of rows of 64 k (128 B), 8-row groups 1024 B
       //            apart (SBO); a K step of 16 elements is 32 B inside the
@@ -511,21 +536,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                   // start-address field is bits [0,14) in 16-byte units
                   const uint64_t da = da0 + (uint64_t)(a_off(kk) >> 4);
                   const uint64_t db = db0 + (uint64_t)(b_off(kk) >> 4);
-                  const uint32_t dd = d_tmem;
-                  if constexpr (G == 2)
-                    umma_f16_pair(dd, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-                  else
-                    umma_f16(dd, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                  for (int h = 0; h < Cf::kMmaPerK; ++h) {
+                    const uint32_t dd = d_tmem + (uint32_t)(h * Cf::kMmaN);
+                    const uint64_t dbh = db + (uint64_t)((h * Cf::kBHalf) >> 4);
+                    if constexpr (G == 2)
+                      umma_f16_pair(dd, da, dbh, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    else
+                      umma_f16(dd, da, dbh, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                  }
                 }
               } else {
                 const int nk16 = (kvalid + 15) / 16;
                 for (int kk = 0; kk < nk16; ++kk) {
                   const uint64_t da = da0 + (uint64_t)(a_off(kk) >> 4);
                   const uint64_t db = db0 + (uint64_t)(b_off(kk) >> 4);
-                  if constexpr (G == 2)
-                    umma_f16_pair(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-                  else
-                    umma_f16(d_tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                  for (int h = 0; h < Cf::kMmaPerK; ++h) {
+                    const uint32_t dd = d_tmem + (uint32_t)(h * Cf::kMmaN);
+                    const uint64_t dbh = db + (uint64_t)((h * Cf::kBHalf) >> 4);
+                    if constexpr (G == 2)
+                      umma_f16_pair(dd, da, dbh, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    else
+                      umma_f16(dd, da, dbh, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                  }
                 }
               }
               if constexpr (G == 2) umma_commit_pair(smem_addr(&empty[stage]), 0x3);
@@ -549,8 +582,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           __syncwarp();
         }
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
+        if (++acc == Cf::kAccs) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
       }
       if (lane == 0) {
         TB_PROF_ADD(1, prof_full);
@@ -702,8 +737,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (G == 2) mbar_arrive_cluster(tempty_leader0 + acc * 8);
         else mbar_arrive(smem_addr(&tempty[acc]));
       }
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
+      if (++acc == Cf::kAccs) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
     }
     if (lane == 0 && q == 0) TB_PROF_ADD(3, prof_tf);
     // Outstanding TMA stores must finish before the CTA (and its shared
@@ -883,7 +920,7 @@ tbStatus encode_f16_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t
 }
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumTiles = 5;
+constexpr int kNumTiles = 6;
 std::atomic<bool> g_attr_set[kNumTiles][2][kMaxDevices];
 
 template <int BN, int G, typename OutT>
@@ -927,6 +964,7 @@ tbStatus dispatch_tile(const tb_matmul_plan* plan, const CUtensorMap& ta, const 
     case kTile128x256: return launch_gemm<256, 1, OutT>(plan, ta, tb_, tc, kp, stream, 2, ot);
     case kTile256x128: return launch_gemm<128, 2, OutT>(plan, ta, tb_, tc, kp, stream, 3, ot);
     case kTile256x256: return launch_gemm<256, 2, OutT>(plan, ta, tb_, tc, kp, stream, 4, ot);
+    case kTile256x512: return launch_gemm<512, 2, OutT>(plan, ta, tb_, tc, kp, stream, 5, ot);
   }
   return tb_fail(TB_ERR_UNSUPPORTED, "unknown kernel tile");
 }
@@ -956,6 +994,7 @@ size_t tb_kernel_smem_bytes(int32_t kernel_tile, int32_t /*stages*/) {
     case kTile128x256: return Cfg<256, 1>::kSmem;
     case kTile256x128: return Cfg<128, 2>::kSmem;
     case kTile256x256: return Cfg<256, 2>::kSmem;
+    case kTile256x512: return Cfg<512, 2>::kSmem;
   }
   return 0;
 }
@@ -967,6 +1006,7 @@ int32_t tb_kernel_kb(int32_t kernel_tile) {
     case kTile128x256: return Cfg<256, 1>::kKB;
     case kTile256x128: return Cfg<128, 2>::kKB;
     case kTile256x256: return Cfg<256, 2>::kKB;
+    case kTile256x512: return Cfg<512, 2>::kKB;
   }
   return 0;
 }
@@ -978,6 +1018,7 @@ int32_t tb_kernel_max_stages(int32_t kernel_tile) {
     case kTile128x256: return Cfg<256, 1>::kStages;
     case kTile256x128: return Cfg<128, 2>::kStages;
     case kTile256x256: return Cfg<256, 2>::kStages;
+    case kTile256x512: return Cfg<512, 2>::kStages;
   }
   return 0;
 }
@@ -1052,8 +1093,9 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   else                // storage m × k: [128 m × 64 k] boxes
     st = encode_f16_2d(&ta, A, d.m, d.k, lda, kCtaM, "A");
   if (st != TB_OK) return st;
-  if (d.b_col_major)  // storage n × k (k contiguous): [BN/G n × 64 k] boxes
-    st = encode_f16_2d(&tbm, B, d.n, d.k, ldb, (uint32_t)(plan->cta_n / plan->ctas_per_tile), "B");
+  if (d.b_col_major)  // storage n × k (k contiguous): [BN/G n × 64 k] boxes (at most 128 n)
+    st = encode_f16_2d(&tbm, B, d.n, d.k, ldb,
+                       (uint32_t)std::min(128, plan->cta_n / plan->ctas_per_tile), "B");
   else                // storage k × n: [64 k × 64 n] boxes
     st = encode_f16_2d(&tbm, B, d.k, d.n, ldb, (uint32_t)plan->kb, "B");
   if (st != TB_OK) return st;

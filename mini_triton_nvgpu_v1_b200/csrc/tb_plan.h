@@ -18,6 +18,7 @@ enum TbKernelTile : int32_t {
   kTile128x256 = 2,
   kTile256x128 = 3,  // CTA pair (cta_group::2)
   kTile256x256 = 4,  // CTA pair (cta_group::2)
+  kTile256x512 = 5,  // CTA pair, two N = 256 MMAs per K step, one accumulator
 };
 
 enum TbEpilogue : int32_t {

@@ -75,6 +75,15 @@ CASES = [
      "normal", 4),
     ("pair256x256_ragged", (1000, 1000, 520), dict(block_m=256, block_n=256, block_k=64,
                                                    exact_tile=False), "uniform", 11),
+    ("pair256x512_grouped", (1024, 2048, 1024), dict(block_m=256, block_n=512, block_k=64, group_m=8),
+     "normal", 4),
+    ("pair256x512_ragged", (1000, 1300, 520), dict(block_m=256, block_n=512, block_k=64,
+                                                   exact_tile=False), "uniform", 11),
+    ("pair256x384_split_serial", (512, 768, 2048), dict(block_m=128, block_n=384, block_k=64,
+                                                        split_k=4, reduction_mode="split_k_serial"),
+     "uniform", 13),
+    ("pair256x512_persistent", (768, 1536, 256), dict(block_m=256, block_n=512, block_k=64,
+                                                      persistent=True, num_ctas=5), "uniform", 14),
     ("pair256x128_ragged_k_tail", (300, 200, 72), dict(block_m=256, block_n=128, block_k=16,
                                                        exact_tile=False), "uniform", 13),
     ("pair_block192x200", (800, 640, 256), dict(block_m=192, block_n=200, block_k=64,

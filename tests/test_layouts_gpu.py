@@ -19,6 +19,7 @@ KNOBS = [
     ((96, 80, 40), dict(block_m=64, block_n=64, block_k=16, exact_tile=False)),
     ((512, 512, 4096), dict(block_m=256, block_n=256, block_k=64, split_k=8,
                             reduction_mode="split_k_serial")),
+    ((1000, 1200, 520), dict(block_m=256, block_n=512, block_k=64, exact_tile=False)),
 ]
 
 

@@ -76,7 +76,7 @@ def test_unsupported_tiles_are_reported():
         plan(1024, 1024, 64, 512, 64, 32)
     assert e.value.code == 2
     with pytest.raises(tb.TBError) as e:
-        plan(1024, 1024, 64, 128, 512, 32)
+        plan(1024, 1024, 64, 128, 640, 32, exact_tile=False)
     assert e.value.code == 2
 
 
@@ -200,6 +200,11 @@ def test_hardware_tile_selection():
     info = plan(8192, 8192, 8192, 256, 256, 64).info
     assert info["kernel"] == "tb_gemm_sm100_pair_256x256" and info["ctas_per_tile"] == 2
     assert info["grid"] == 148 and info["tmem_cols"] == 512 and info["smem_bytes"] <= 232448
+    # block_n in (256, 512]: one 256 × 512 pair accumulator (two N = 256 MMAs)
+    for bm, bn in ((256, 512), (128, 384)):
+        info = plan(8192, 8192, 8192, bm, bn, 64, exact_tile=False).info
+        assert info["kernel"] == "tb_gemm_sm100_pair_256x512" and info["tmem_cols"] == 512
+        assert info["cta_tile"] == [256, 512, 64] and info["smem_bytes"] <= 232448
 
 
 # ------------------------------------------- the reference's FileCheck facts
