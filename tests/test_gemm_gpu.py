@@ -75,6 +75,12 @@ CASES = [
      "normal", 4),
     ("pair256x256_ragged", (1000, 1000, 520), dict(block_m=256, block_n=256, block_k=64,
                                                    exact_tile=False), "uniform", 11),
+    ("skinny_parallel_512x512x16384", (512, 512, 16384), dict(block_m=256, block_n=256, block_k=64,
+                                                              split_k=16, reduction_mode="split_k_parallel"),
+     "uniform", 15),
+    ("ragged_parallel_700x300x9000", (700, 300, 9000), dict(block_m=128, block_n=128, block_k=32, split_k=3,
+                                                            reduction_mode="split_k_parallel",
+                                                            exact_tile=False), "uniform", 16),
     ("pair256x512_grouped", (1024, 2048, 1024), dict(block_m=256, block_n=512, block_k=64, group_m=8),
      "normal", 4),
     ("pair256x512_ragged", (1000, 1300, 520), dict(block_m=256, block_n=512, block_k=64,
