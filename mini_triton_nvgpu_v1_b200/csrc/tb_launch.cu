@@ -159,7 +159,7 @@ struct KParams {
   int32_t vec_ws;    // workspace rows allow 16-byte vector access
   int32_t tma_out;   // TmaOut: f32 tile output written by TMA from swizzled shared staging
   int32_t fuse;      // program pairing (plan.fuse): work item w runs programs 2w and 2w+1
-  int32_t walk_grouped;  // row-major mapping walked in row groups (walk_item)
+  int32_t walk_grouped;  // 1: row-major mapping walked in row groups; 2: GROUP_M serpentine (walk_item)
   int32_t work_items;
   EpiExprs ex;       // applied in kEpiStore (split_k_serial: in the reduction)
   int32_t a_mn;      // A stored M-major (column-major m × k): MN-major UMMA operand
@@ -231,6 +231,21 @@ struct Extent {
 constexpr int32_t kWalkRows = 8;
 
 __device__ __forceinline__ int32_t walk_item(const KParams& p, int32_t w) {
+  if (p.walk_grouped == 2) {
+    // GROUP_M order, every other group walked from its last column back:
+    // the first programs of a group reuse the B panels the previous group
+    // read last. Items are programs, or vertical pairs (fuse == 1).
+    const int32_t per = p.fuse == 1 ? 2 : 1;
+    const int32_t ppg = p.map.programs_per_group / per;  // items per full group
+    const int32_t g = w / ppg;
+    if ((g & 1) == 0) return w;
+    const int32_t first = g * p.map.group_span_m;
+    const int32_t left = p.map.tiles_m - first;
+    const int32_t size = (left < p.map.group_span_m ? left : p.map.group_span_m) / per;
+    const int32_t in = w - g * ppg;
+    const int32_t c = in / size, r = in % size;
+    return g * ppg + (p.map.tiles_n - 1 - c) * size + r;
+  }
   if (!p.walk_grouped) return w;
   const int32_t cols = p.map.tiles_n / (p.fuse == 2 ? 2 : 1);
   const int32_t span = kWalkRows * cols;
@@ -1148,6 +1163,7 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   kp.fuse = plan->fuse;
   kp.walk_grouped = (kp.map.kind == tb::kMapTile || kp.map.kind == tb::kMapPersistentTile) &&
                     kp.map.tiles_m > 1 && kp.map.tiles_n / (plan->fuse == 2 ? 2 : 1) > 1;
+  if (kp.map.kind == tb::kMapGroupedTile) kp.walk_grouped = 2;
   kp.work_items = (int32_t)plan->work_items;
   kp.a_mn = d.a_col_major ? 1 : 0;
   kp.b_kmaj = d.b_col_major ? 1 : 0;
