@@ -159,7 +159,7 @@ struct KParams {
   int32_t vec_ws;    // workspace rows allow 16-byte vector access
   int32_t tma_out;   // TmaOut: f32 tile output written by TMA from swizzled shared staging
   int32_t fuse;      // program pairing (plan.fuse): work item w runs programs 2w and 2w+1
-  int32_t walk_grouped;  // 1: row-major mapping walked in row groups; 2: GROUP_M serpentine (walk_item)
+  int32_t walk_grouped;  // tb::WalkMode: the order resident CTAs take work items in
   int32_t work_items;
   EpiExprs ex;       // applied in kEpiStore (split_k_serial: in the reduction)
   int32_t a_mn;      // A stored M-major (column-major m × k): MN-major UMMA operand
@@ -221,43 +221,8 @@ struct Extent {
   int32_t m0, n0, rows, cols, k_begin, k_end, nkb, part;
 };
 
-// Hardware order of work items for row-major / persistent mappings. The
-// reference's persistent CTAs take row-major pids c, c + R, ... — every
-// concurrent wave then spans a full row of tiles and re-reads the B panels
-// from DRAM for each tile row. Which resident CTA runs a program does not
-// change its result, so the items (a program, or a horizontal pair) are
-// walked in groups of kWalkRows item rows, column by column, as GROUP_M
-// does; each program still computes exactly the reference's tile.
-constexpr int32_t kWalkRows = 8;
-
-__device__ __forceinline__ int32_t walk_item(const KParams& p, int32_t w) {
-  if (p.walk_grouped == 2) {
-    // GROUP_M order, every other group walked from its last column back:
-    // the first programs of a group reuse the B panels the previous group
-    // read last. Items are programs, or vertical pairs (fuse == 1).
-    const int32_t per = p.fuse == 1 ? 2 : 1;
-    const int32_t ppg = p.map.programs_per_group / per;  // items per full group
-    const int32_t g = w / ppg;
-    if ((g & 1) == 0) return w;
-    const int32_t first = g * p.map.group_span_m;
-    const int32_t left = p.map.tiles_m - first;
-    const int32_t size = (left < p.map.group_span_m ? left : p.map.group_span_m) / per;
-    const int32_t in = w - g * ppg;
-    const int32_t c = in / size, r = in % size;
-    return g * ppg + (p.map.tiles_n - 1 - c) * size + r;
-  }
-  if (!p.walk_grouped) return w;
-  const int32_t cols = p.map.tiles_n / (p.fuse == 2 ? 2 : 1);
-  const int32_t span = kWalkRows * cols;
-  const int32_t first = (w / span) * kWalkRows;
-  const int32_t left = p.map.tiles_m - first;
-  const int32_t size = left < kWalkRows ? left : kWalkRows;
-  const int32_t in = w % span;
-  return (first + in % size) * cols + in / size;
-}
-
 __device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pid, int32_t kb) {
-  const int32_t item = walk_item(p, pid);
+  const int32_t item = tb::walk_item(p.map, p.fuse, p.walk_grouped, pid);
   const tb::Work w = tb::program_work(p.map, p.fuse ? 2 * item : item);
   Extent e;
   e.m0 = w.tile_m * p.block_m;
@@ -1161,9 +1126,7 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   kp.epilogue = plan->epilogue;
   kp.beta = d.beta ? 1 : 0;
   kp.fuse = plan->fuse;
-  kp.walk_grouped = (kp.map.kind == tb::kMapTile || kp.map.kind == tb::kMapPersistentTile) &&
-                    kp.map.tiles_m > 1 && kp.map.tiles_n / (plan->fuse == 2 ? 2 : 1) > 1;
-  if (kp.map.kind == tb::kMapGroupedTile) kp.walk_grouped = 2;
+  kp.walk_grouped = tb::walk_mode(kp.map, plan->fuse);
   kp.work_items = (int32_t)plan->work_items;
   kp.a_mn = d.a_col_major ? 1 : 0;
   kp.b_kmaj = d.b_col_major ? 1 : 0;

@@ -69,4 +69,53 @@ TB_HD Work program_work(const MappingArgs& a, int32_t pid) {
   return w;
 }
 
+// ---- hardware walk order ----------------------------------------------
+// The order in which resident CTAs take work items (a program, or a pair of
+// programs when the plan fuses them: fuse 1 = pids 2w, 2w+1 vertical, 2 =
+// horizontal). Which CTA runs a program, and when, does not change its
+// result: each program still computes the reference's tile over its K range.
+// The order only decides what shares L2 at a time.
+//   kWalkRowGroups (row-major tile / persistent mappings): the reference's
+//     persistent CTAs take pids c, c + R, ..., so every concurrent wave spans
+//     a full tile row and re-reads each B panel from DRAM per tile row. Items
+//     are walked in groups of kWalkRows item rows, column by column.
+//   kWalkSerpentine (grouped mapping): GROUP_M order, every other group
+//     walked from its last column back, so a group's first programs reuse the
+//     B panels the previous group read last.
+enum WalkMode : int32_t { kWalkIdentity = 0, kWalkRowGroups = 1, kWalkSerpentine = 2 };
+constexpr int32_t kWalkRows = 8;
+
+TB_HD int32_t walk_mode(const MappingArgs& a, int32_t fuse) {
+  if (a.kind == kMapGroupedTile) return kWalkSerpentine;
+  if ((a.kind == kMapTile || a.kind == kMapPersistentTile) && a.tiles_m > 1 &&
+      a.tiles_n / (fuse == 2 ? 2 : 1) > 1)
+    return kWalkRowGroups;
+  return kWalkIdentity;
+}
+
+// Work item taken at position `w` of the walk.
+TB_HD int32_t walk_item(const MappingArgs& a, int32_t fuse, int32_t mode, int32_t w) {
+  if (mode == kWalkSerpentine) {
+    const int32_t per = fuse == 1 ? 2 : 1;               // programs per item
+    const int32_t ppg = a.programs_per_group / per;      // items per full group
+    const int32_t g = w / ppg;
+    if ((g & 1) == 0) return w;
+    const int32_t first = g * a.group_span_m;
+    const int32_t left = a.tiles_m - first;
+    const int32_t size = (left < a.group_span_m ? left : a.group_span_m) / per;
+    const int32_t in = w - g * ppg;
+    return g * ppg + (a.tiles_n - 1 - in / size) * size + in % size;
+  }
+  if (mode == kWalkRowGroups) {
+    const int32_t cols = a.tiles_n / (fuse == 2 ? 2 : 1);
+    const int32_t span = kWalkRows * cols;
+    const int32_t first = (w / span) * kWalkRows;
+    const int32_t left = a.tiles_m - first;
+    const int32_t size = left < kWalkRows ? left : kWalkRows;
+    const int32_t in = w % span;
+    return (first + in % size) * cols + in / size;
+  }
+  return w;
+}
+
 }  // namespace tb

@@ -471,6 +471,10 @@ extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* bu
   o << "\"fused_program_pairs\": \"" << (plan->fuse == 1 ? "vertical" : plan->fuse == 2 ? "horizontal" : "none")
     << "\", ";
   o << "\"work_items\": " << plan->work_items << ", ";
+  {
+    const char* walks[] = {"program_order", "row_groups", "serpentine_groups"};
+    o << "\"hardware_walk\": \"" << walks[tb::walk_mode(plan->map, plan->fuse)] << "\", ";
+  }
   o << "\"stages\": " << plan->stages << ", ";
   o << "\"smem_bytes\": " << plan->smem_bytes << ", ";
   o << "\"tmem_cols\": " << plan->tmem_cols << ", ";
