@@ -220,6 +220,32 @@ tbStatus tb_matmul_run_kshard_peer(const tb_matmul_plan* plan, tb_peer_comm* com
 tbStatus tb_peer_comm_status(tb_peer_comm* comm, void* stream, uint32_t* raw);
 tbStatus tb_peer_comm_destroy(tb_peer_comm* comm);
 
+/* ---- K-sharded runs with an NCCL reduce-scatter (one process per GPU) ----
+ * The same partition as tb_matmul_run_kshard_peer, with the cross-GPU sum
+ * done by ncclReduceScatter: rank r runs its K slice (plan: m × n × k_r, f32
+ * C, any reduction mode) into an f32 staging copy of C held in `workspace`
+ * (its own rows seeded with C_in when beta = 1, the rest zero), then the
+ * staging buffers are reduce-scattered so C_rows (rank r's m/W rows, row
+ * stride ldc) ends as C_rows_in + Σ_r A_r·B_r. Replaces the split-K reduction
+ * of ReductionPlan.cpp:137-192 / LowerPipelineToNVGPU.cpp:1862-1912 across
+ * GPUs. NCCL is loaded at run time (libnccl.so.2); TB_ERR_NCCL when absent.
+ * The communicator is this library's (tb_nccl_comm_create from a unique id
+ * that rank 0 makes and the caller distributes). */
+typedef struct tb_nccl_comm tb_nccl_comm;
+tbStatus tb_nccl_unique_id(unsigned char id[128]);
+tbStatus tb_nccl_comm_create(int rank, int world, const unsigned char id[128],
+                             tb_nccl_comm** comm);
+tbStatus tb_nccl_comm_destroy(tb_nccl_comm* comm);
+/* Workspace bytes of tb_matmul_run_kshard_nccl (staging + plan workspace). */
+size_t tb_matmul_kshard_nccl_workspace_bytes(const tb_matmul_plan* plan, int world,
+                                             int64_t ldc);
+/* Collective: every rank calls it with plans of the same m × n. */
+tbStatus tb_matmul_run_kshard_nccl(const tb_matmul_plan* plan, tb_nccl_comm* comm,
+                                   const void* A, int64_t lda, const void* B,
+                                   int64_t ldb, void* C_rows, int64_t ldc,
+                                   void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
 /* tb_matmul_run with the bias of a plan made with desc.bias = 1 (`bias`:
  * n f32 values, one per column of C; NULL when the plan has no bias). */
 tbStatus tb_matmul_run_epilogue(const tb_matmul_plan* plan, const void* A,

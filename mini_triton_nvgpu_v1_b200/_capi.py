@@ -107,6 +107,13 @@ PROTOTYPES = {
                                             C.c_int64, C.c_void_p]),
     "tb_peer_comm_status": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_uint32)]),
     "tb_peer_comm_destroy": (C.c_int, [C.c_void_p]),
+    "tb_nccl_unique_id": (C.c_int, [C.c_char_p]),
+    "tb_nccl_comm_create": (C.c_int, [C.c_int, C.c_int, C.c_char_p, C.POINTER(C.c_void_p)]),
+    "tb_nccl_comm_destroy": (C.c_int, [C.c_void_p]),
+    "tb_matmul_kshard_nccl_workspace_bytes": (C.c_size_t, [C.c_void_p, C.c_int, C.c_int64]),
+    "tb_matmul_run_kshard_nccl": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p,
+                                            C.c_int64, C.c_void_p, C.c_int64, C.c_void_p, C.c_size_t,
+                                            C.c_void_p]),
     "tb_selftest_bounded_wait": (C.c_int, [C.c_void_p, C.c_uint64]),
     "tb_device_status": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32)]),
     "tb_last_error": (C.c_char_p, []),

@@ -17,7 +17,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libtbgemm.so"
 
-SOURCES = ["tb_plan.cpp", "tb_dynamic.cpp", "tb_launch.cu", "tb_peer.cu"]
+SOURCES = ["tb_plan.cpp", "tb_dynamic.cpp", "tb_launch.cu", "tb_peer.cu", "tb_nccl.cpp"]
 HEADERS = ["tb_plan.h", "tb_mapping.h", "tb_sm100.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

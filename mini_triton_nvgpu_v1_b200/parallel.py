@@ -154,3 +154,58 @@ class PeerKShard:
         if getattr(self, "_h", None) is not None and self._h.value:
             self._lib.tb_peer_comm_destroy(self._h)
             self._h = None
+
+
+class NcclKShard:
+    """K-sharded tb.matmul through the C ABI's NCCL path
+    (tb_matmul_run_kshard_nccl): each rank's K-slice GEMM runs into an f32
+    staging copy of C, then one ncclReduceScatter leaves every rank its rows.
+
+    C_rows: this rank's [m / world, n] f32 rows of C (CUDA memory, unit minor
+    stride), updated in place by every run. The constructor is collective: rank
+    0 makes the NCCL unique id and `group` (any torch.distributed backend)
+    carries it to the others."""
+
+    def __init__(self, C_rows, group=None):
+        import ctypes as C
+        import torch.distributed as dist
+        from . import _check, _load_lib
+        self._lib = _load_lib()
+        self._check = _check
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if C_rows.dtype.itemsize != 4 or C_rows.stride(1) != 1 or not C_rows.is_cuda:
+            raise ValueError("C_rows must be an f32 CUDA tensor with unit minor stride")
+        self.C_rows = C_rows
+        uid = C.create_string_buffer(128)
+        if self.rank == 0:
+            _check(self._lib.tb_nccl_unique_id(uid))
+        box = [bytes(uid.raw)]
+        dist.broadcast_object_list(box, src=0 if group is None else dist.get_global_rank(group, 0),
+                                   group=group)
+        self._h = C.c_void_p()
+        _check(self._lib.tb_nccl_comm_create(self.rank, self.world, box[0], C.byref(self._h)))
+        self._ws = None
+
+    def run(self, plan, A_local, B_local, stream=None):
+        """C_rows ← C_rows + Σ_ranks A_local·B_local restricted to these rows
+        (beta = 1 plans; beta = 0 gives the sum alone). `plan`: MatmulPlan of
+        the local problem (m × n × k_local)."""
+        import ctypes as C
+        import torch
+        need = int(self._lib.tb_matmul_kshard_nccl_workspace_bytes(plan._h, self.world,
+                                                                    self.C_rows.stride(0)))
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.C_rows.device)
+        s = stream if stream is not None else torch.cuda.current_stream(A_local.device)
+        lda = A_local.stride(1) if plan.cfg.a_col_major else A_local.stride(0)
+        ldb = B_local.stride(1) if plan.cfg.b_col_major else B_local.stride(0)
+        self._check(self._lib.tb_matmul_run_kshard_nccl(
+            plan._h, self._h, C.c_void_p(A_local.data_ptr()), lda, C.c_void_p(B_local.data_ptr()), ldb,
+            C.c_void_p(self.C_rows.data_ptr()), self.C_rows.stride(0), C.c_void_p(self._ws.data_ptr()),
+            self._ws.numel(), C.c_void_p(s.cuda_stream or None)))
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            self._lib.tb_nccl_comm_destroy(self._h)
+            self._h = None

@@ -85,3 +85,16 @@ def test_describe_reports_buffer_size():
 
 def test_version_string():
     assert b"sm_100a" in _capi.load().tb_version()
+
+
+def test_kshard_nccl_rejects_bad_arguments_before_any_cuda_call():
+    import mini_triton_nvgpu_v1_b200 as tb
+    lib = _capi.load()
+    plan = tb.MatmulPlan(tb.KernelConfig(m=512, n=512, k=1024, block_m=128, block_n=128, block_k=64))
+    st = lib.tb_matmul_run_kshard_nccl(plan._h, None, None, 0, None, 0, None, 512, None, 0, None)
+    assert st == _capi.TB_ERR_INVALID_ARGUMENT
+    # staging m × n f32 (+ receive rows when ldc != n) + the plan's own workspace
+    assert lib.tb_matmul_kshard_nccl_workspace_bytes(plan._h, 2, 512) == 512 * 512 * 4
+    assert lib.tb_matmul_kshard_nccl_workspace_bytes(plan._h, 2, 520) == 512 * 512 * 4 + 256 * 512 * 4
+    h = C.c_void_p()
+    assert lib.tb_nccl_comm_create(3, 2, b"\0" * 128, C.byref(h)) == _capi.TB_ERR_INVALID_ARGUMENT

@@ -55,7 +55,18 @@ def _worker(rank, world, port, q, m, n, k, knobs):
                                            if kk not in ("split_k", "reduction_mode")})
         err2 = float(np.abs(rows2.cpu().numpy() - once[r0:r0 + mr]).max())
         comm.close()
-        q.put((rank, err, err2, oracle.tolerance(k)))
+        # the C ABI's NCCL path (tb_matmul_run_kshard_nccl), into a strided view of C rows
+        wide = torch.zeros(mr, n + 8, device=dev)
+        wide[:, :n] = torch.from_numpy(Cin[r0:r0 + mr].copy()).to(dev)
+        rows3 = wide[:, :n]
+        nc = par.NcclKShard(rows3)
+        for _ in range(2):
+            nc.run(plan, tA, tB)
+        torch.cuda.synchronize()
+        nc.close()
+        err3 = float(np.abs(rows3.cpu().numpy() - want).max())
+        assert float(wide[:, n:].abs().max()) == 0.0          # nothing written past n
+        q.put((rank, max(err, err3), err2, oracle.tolerance(k)))
     finally:
         dist.destroy_process_group()
 
