@@ -54,9 +54,10 @@ def parse():
     ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "splitk", "sweep"],
                     help="gemm8192: the headline 8192^3 N-sharded GEMM; splitk: the skinny "
                          "512x512x65536 split-K config (K-sharded + reduce-scatter at N>1)")
-    ap.add_argument("--kshard", default="peer", choices=["peer", "nccl"],
-                    help="splitk at N>1: reduce-scatter fused into the GEMM over NVLink (peer) "
-                         "or an NCCL reduce-scatter after it")
+    ap.add_argument("--kshard", default="peer", choices=["peer", "capi", "nccl"],
+                    help="splitk at N>1: reduce-scatter fused into the GEMM over NVLink (peer), "
+                         "the C ABI's NCCL reduce-scatter run (capi), or torch.distributed's "
+                         "reduce-scatter after the GEMM (nccl)")
     return ap.parse_args()
 
 
@@ -405,7 +406,9 @@ def run_splitk(args):
     C_rows = torch.zeros(mr, SK_N, device=dev)
     partial = torch.zeros(SK_M, SK_N, device=dev)
     recv = torch.empty_like(C_rows)
+    capi = world > 1 and args.kshard == "capi"
     comm = par.PeerKShard(C_rows) if peer else None
+    ncomm = par.NcclKShard(C_rows) if capi else None
 
     def step():
         if world == 1:
@@ -413,6 +416,8 @@ def run_splitk(args):
                          SK_N, ws.data_ptr(), ws.numel(), stream.cuda_stream)
         elif peer:
             comm.run(plan, A, B)
+        elif capi:
+            ncomm.run(plan, A, B)
         else:
             partial.zero_()
             plan.run_ptr(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), partial.data_ptr(),
@@ -450,16 +455,18 @@ def run_splitk(args):
             "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "strong", "dtype": "f16", "data": "synthetic",
             "config": {"workload": f"tb.matmul {SK_M}x{SK_N}x{SK_K} split_k={SK_SPLIT} "
-                                   f"({('K-shard x%d, reduce-scatter fused into the GEMM over NVLink' if peer else 'K-shard x%d + NCCL reduce-scatter') % world if world > 1 else '1 GPU'})",
+                                   f"({('K-shard x%d, reduce-scatter fused into the GEMM over NVLink' if peer else 'K-shard x%d, tb_matmul_run_kshard_nccl' if capi else 'K-shard x%d + NCCL reduce-scatter') % world if world > 1 else '1 GPU'})",
                        "split_k_per_rank": split_local, "kernel": plan.info["kernel"]},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(gbs / hbm, 4),
                          "note": "algorithmic bytes per GPU (its A/B K-slice + C_in + C) / step time"},
-            "gpu_launches": args.steps * (2 if world == 1 else 3 if peer else 4),
+            "gpu_launches": args.steps * (2 if world == 1 else 3 if peer else 2),
         }), flush=True)
     if comm is not None:
         comm.check()
         comm.close()
+    if ncomm is not None:
+        ncomm.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
