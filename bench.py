@@ -504,8 +504,10 @@ SWEEP = [
 
 def run_sweep(args):
     """One JSON line per BASELINE config: device time per call (CUDA events,
-    ~0.3 s of back-to-back calls after warm-up, best of 3), TFLOP/s and the
-    fraction of the roofline that bounds the config."""
+    ~0.3 s of back-to-back calls after warm-up, best of 3), the distribution
+    of 21 calls timed one at a time (median / min / max / spread), the
+    CUDA-graph time per call, TFLOP/s and the fraction of the roofline that
+    bounds the config."""
     import torch
     import mini_triton_nvgpu_v1_b200 as tb
     dev = torch.device("cuda", 0)
@@ -538,6 +540,21 @@ def run_sweep(args):
             e1.record()
             torch.cuda.synchronize()
             best = min(best, e0.elapsed_time(e1) / reps)
+        # per-call distribution (each call timed alone, stream idle before it):
+        # median / min / max / spread, as the reference's bench reports them
+        single = []
+        for _ in range(21):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            f()
+            e1.record()
+            torch.cuda.synchronize()
+            single.append(e0.elapsed_time(e1) * 1e3)
+        single.sort()
+        med = single[len(single) // 2]
+        per_call = {"median": round(med, 2), "min": round(single[0], 2), "max": round(single[-1], 2),
+                    "spread_pct": round(100.0 * (single[-1] - single[0]) / med, 1)}
         tb.device_status()
         # device-only time per call: replay a CUDA graph of back-to-back calls
         graph_us = None
@@ -574,7 +591,8 @@ def run_sweep(args):
         alg_bytes = 2.0 * (m * k + k * n) + 2 * cb * m * n
         line = {"workload": "sweep", "config": name, "us": round(best * 1e3, 2), "graph_us": graph_us,
                 "tflops": round(flops / (best * 1e-3) / 1e12, 2),
-                "gbs": round(alg_bytes / (best * 1e-3) / 1e9, 1), "bound": bound}
+                "gbs": round(alg_bytes / (best * 1e-3) / 1e9, 1), "bound": bound,
+                "single_call_us": per_call}
         if bound == "tensor":
             line["frac_of_sustained_peak"] = round(line["tflops"] / peak_s, 3)
         elif bound == "hbm":
