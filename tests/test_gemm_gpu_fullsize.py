@@ -167,3 +167,31 @@ def test_deterministic_serial_split_k(cuda):
                   reduction_mode="split_k_serial")
         outs.append(c)
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+
+
+@pytest.mark.parametrize("col_major_a", [False, True])
+def test_operands_past_4_gib(cuda, col_major_a):
+    """An A of 2^31 f16 elements (4 GiB): rows far past the 32-bit byte range
+    (TMA coordinates and epilogue row offsets in 64-bit arithmetic), in both
+    A layouts, checked on sampled rows including the last ones."""
+    import torch
+    import mini_triton_nvgpu_v1_b200 as tb
+    import oracle
+    m, n, k = 131072, 256, 16384
+    g = torch.Generator(device=cuda).manual_seed(21)
+    if col_major_a:
+        tA = ((torch.rand(k, m, device=cuda, generator=g) * 2 - 1).half()).t()   # m × k, unit row stride
+    else:
+        tA = (torch.rand(m, k, device=cuda, generator=g) * 2 - 1).half()
+    tB = (torch.rand(k, n, device=cuda, generator=g) * 2 - 1).half()
+    tC = torch.randn(m, n, device=cuda, generator=g)
+    C0 = tC.clone()
+    tb.matmul(tA, tB, tC, block_m=256, block_n=256, block_k=64)
+    torch.cuda.synchronize()
+    assert tb.device_status() == 0
+    rows = np.array([0, 1, 8191, 65535, 65536, 100000, 131071 - 255, 131070, 131071])
+    ridx = torch.from_numpy(rows).to(cuda)
+    A_rows = tA[ridx].contiguous().cpu().numpy()
+    ref = oracle.matmul_ref(A_rows, tB.cpu().numpy(), C0[ridx].cpu().numpy())
+    err = float(np.abs(tC[ridx].cpu().numpy() - ref).max())
+    assert err <= oracle.tolerance(k), err
