@@ -159,6 +159,7 @@ struct KParams {
   int32_t vec_ws;    // workspace rows allow 16-byte vector access
   int32_t tma_out;   // TmaOut: f32 tile output written by TMA from swizzled shared staging
   int32_t fuse;      // program pairing (plan.fuse): work item w runs programs 2w and 2w+1
+  int32_t cin_smem;  // one work item per CTA: the epilogue stages C_in through the idle ring
   int32_t walk_grouped;  // tb::WalkMode: the order resident CTAs take work items in
   int32_t work_items;
   EpiExprs ex;       // applied in kEpiStore (split_k_serial: in the reduction)
@@ -638,6 +639,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const bool row_ok = row_in_tile < e.rows;
       const int64_t grow = (int64_t)e.m0 + row_in_tile;
+      // When each CTA has a single work item, the mainloop's ring is idle
+      // once tfull arrives (every MMA that read it has completed, and no
+      // load follows). Each thread then copies its whole C_in row into it
+      // with cp.async — all 16-byte pieces in flight at once — instead of one
+      // DRAM round trip per 32-column chunk (a clock64 timeline of a
+      // single-wave 2048³ launch showed ~1.3k of each chunk's ~1.7k cycles
+      // waiting on that load). Rows are padded by 16 bytes: the warp's
+      // per-row reads then spread over all banks.
+      constexpr uint32_t kCinStride = (uint32_t)(BN * sizeof(OutT)) + 16u;
+      constexpr bool kCinFits = 128u * kCinStride <= (uint32_t)S * Cf::kStageBytes;
+      const bool cin_from_smem = kCinFits && p.cin_smem && p.beta && p.epilogue == kEpiStore && row_ok;
+      const uint8_t* cin_row = smem + (size_t)((warp - 2) * 32 + lane) * kCinStride;
+      if (cin_from_smem) {
+        fence_proxy_async_smem();
+        const char* src = reinterpret_cast<const char*>(reinterpret_cast<const OutT*>(p.C) +
+                                                        grow * p.ldc + e.n0);
+        const int bytes = e.cols * (int)sizeof(OutT);
+        for (int off = 0; off < bytes; off += 16)
+          cp_async_16(smem_addr(cin_row + off), src + off, (uint32_t)min(16, bytes - off));
+        cp_async_wait_all();
+      }
+      // C_in of columns [c0, c0 + 32) of this row (zero past ncol).
+      auto load_cin = [&](int c0, int ncol, float (&c)[32]) {
+        if (cin_from_smem) {
+          if constexpr (sizeof(OutT) == 4) {
+            const float4* q4 = reinterpret_cast<const float4*>(cin_row + c0 * 4);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 t = q4[j];
+              c[4 * j] = t.x; c[4 * j + 1] = t.y; c[4 * j + 2] = t.z; c[4 * j + 3] = t.w;
+            }
+          } else {
+            const __half2* h2 = reinterpret_cast<const __half2*>(cin_row + c0 * 2);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float2 f = __half22float2(h2[j]);
+              c[2 * j] = f.x; c[2 * j + 1] = f.y;
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i >= ncol) c[i] = 0.f;
+          return;
+        }
+        const OutT* src = reinterpret_cast<const OutT*>(p.C) + grow * p.ldc + e.n0 + c0;
+        if (ncol == 32 && (p.vec_c || p.tma_out == kTmaStoreC)) {
+          OutIO<OutT>::load32(src, c);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) c[i] = i < ncol ? OutIO<OutT>::load(src + i) : 0.f;
+        }
+      };
       for (int c0 = 0; c0 < e.cols; c0 += 32) {
         float v[32];
         if (e.nkb > 0) {
@@ -659,14 +712,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 32; ++i) v[i] = 0.f;
           }
           if (p.tma_out == kTmaStoreC && p.beta && row_ok) {
-            const float* src = reinterpret_cast<const float*>(p.C) + grow * p.ldc + gcol;
             float c[32];
-            if (ncol == 32) {
-              OutIO<float>::load32(src, c);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) c[i] = i < ncol ? OutIO<float>::load(src + i) : 0.f;
-            }
+            load_cin(c0, ncol, c);
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] += c[i];
           }
@@ -702,7 +749,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ncol == 32 && p.vec_c) {
             if (p.beta) {
               float c[32];
-              OutIO<OutT>::load32(dst, c);
+              load_cin(c0, ncol, c);
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] += c[i];
             }
@@ -1139,6 +1186,7 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   kp.vec_c = aligned16(Cp) && ((ldc * (int64_t)out_bytes) % 16 == 0) &&
              ((d.block_n * (int64_t)out_bytes) % 16 == 0);
   kp.vec_ws = (d.n % 4 == 0) && (d.block_n % 4 == 0) && aligned16(workspace);
+  kp.cin_smem = plan->work_items <= plan->grid / plan->ctas_per_tile && kp.vec_c;
   kp.C = Cp;
   kp.ldc = ldc;
   kp.ws = reinterpret_cast<float*>(workspace);
