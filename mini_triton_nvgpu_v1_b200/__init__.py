@@ -356,28 +356,35 @@ def matmul(A, B, Cm, *, block_m: int = 128, block_n: int = 256, block_k: int = 6
                            a_col_major=a_col, b_col_major=b_col)
         plan = plan_for(cfg, Cm.device.index if Cm.is_cuda else None)
         _check_tensors(cfg, A, B, Cm)
+        # the bound C entry points and the device index ride along, so a hit
+        # costs a dict lookup, three data_ptr() calls and one ctypes call
         hit = (plan, A.stride(1) if a_col else A.stride(0), B.stride(1) if b_col else B.stride(0),
-               Cm.stride(0), plan.workspace_bytes)
+               Cm.stride(0), plan.workspace_bytes, _lib.tb_matmul_run, _lib.tb_matmul_run_epilogue,
+               Cm.device.index)
         if len(_FAST) > 1024:
             _FAST.clear()
         _FAST[key] = hit
-    plan, lda, ldb, ldc, need = hit
+    plan, lda, ldb, ldc, need, run, run_epilogue, dev_index = hit
     ws_ptr, ws_bytes = 0, 0
     if need:
         if workspace is None:
             workspace = torch.empty(need, dtype=torch.uint8, device=Cm.device)
         ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
-    s = stream if stream is not None else torch.cuda.current_stream(Cm.device)
+    if stream is not None:
+        sp = stream.cuda_stream
+    else:  # the current stream of C's device, as a raw handle
+        sp = torch._C._cuda_getCurrentRawStream(dev_index)
     if bias is not None:
         if bias.dtype != torch.float32 or bias.numel() != Cm.shape[1] or not bias.is_contiguous() \
                 or not bias.is_cuda:
             raise TBError(_capi.TB_ERR_INVALID_ARGUMENT, "bias must be a contiguous f32 CUDA vector of n")
-        _check(_lib.tb_matmul_run_epilogue(plan._h, A.data_ptr(), lda, B.data_ptr(), ldb, Cm.data_ptr(),
-                                           ldc, bias.data_ptr(), ws_ptr or None, ws_bytes,
-                                           s.cuda_stream or None))
+        code = run_epilogue(plan._h, A.data_ptr(), lda, B.data_ptr(), ldb, Cm.data_ptr(), ldc,
+                            bias.data_ptr(), ws_ptr or None, ws_bytes, sp or None)
     else:
-        _check(_lib.tb_matmul_run(plan._h, A.data_ptr(), lda, B.data_ptr(), ldb, Cm.data_ptr(), ldc,
-                                  ws_ptr or None, ws_bytes, s.cuda_stream or None))
+        code = run(plan._h, A.data_ptr(), lda, B.data_ptr(), ldb, Cm.data_ptr(), ldc, ws_ptr or None,
+                   ws_bytes, sp or None)
+    if code:
+        _check(code)
     return Cm
 
 
