@@ -255,3 +255,29 @@ def test_filecheck_facts_cover_the_mapping_contract():
     here include every mapping kind this build plans."""
     kinds = {kv.get("mapping_kind") for f in FACTS.values() for c in f["checks"] for kv in [c["kv"]]}
     assert {"grouped_tile", "split_k", "persistent_tile"} <= kinds
+
+
+# ------------------------------------------------- randomized mapping check
+from hypothesis import assume, given, settings, strategies as st  # noqa: E402
+
+
+@settings(max_examples=150, deadline=None)
+@given(m=st.integers(1, 900), n=st.integers(1, 900), k=st.integers(16, 3000),
+       bm=st.sampled_from([16, 64, 128, 256]), bn=st.sampled_from([8, 64, 128, 256]),
+       bk=st.sampled_from([16, 32, 64]), group_m=st.integers(1, 9), split_k=st.integers(1, 9),
+       persistent=st.booleans(), num_ctas=st.integers(1, 300))
+def test_random_mappings_match_oracle(m, n, k, bm, bn, bk, group_m, split_k, persistent, num_ctas):
+    """Any legal knob set: plan facts and every program's work equal the
+    restatement of ProgramMappingPlan.cpp / LowerPipelineToNVGPU.cpp:279-357."""
+    if persistent:
+        split_k = 1
+    assume(om.warp_grid(4, bm, bn) is not None)   # else the reference rejects the knobs
+    p = plan(m, n, k, bm, bn, bk, group_m=group_m, split_k=split_k, persistent=persistent,
+             num_ctas=num_ctas, exact_tile=False)
+    want = om.program_mapping(m, n, k, bm, bn, bk, group_m=group_m, split_k=split_k,
+                              persistent=persistent, num_ctas=num_ctas)
+    info = p.info
+    assert info["mapping_kind"] == want.kind
+    assert info["total_programs"] == want.total_programs
+    for pid in range(0, want.total_programs, max(1, want.total_programs // 512)):
+        assert p.program_work(pid) == om.program_work(want, pid), pid
