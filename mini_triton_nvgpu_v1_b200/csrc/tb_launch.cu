@@ -1154,9 +1154,10 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   else                // storage m × k: [128 m × 64 k] boxes
     st = encode_f16_2d(&ta, A, d.m, d.k, lda, kCtaM, "A");
   if (st != TB_OK) return st;
-  if (d.b_col_major)  // storage n × k (k contiguous): [BN/G n × 64 k] boxes (at most 128 n)
+  if (d.b_col_major)  // storage n × k (k contiguous): [BN/G n × 64 k] boxes; the 256 × 512
+                      // pair tile loads its 256 columns per CTA as two 128-row boxes
     st = encode_f16_2d(&tbm, B, d.n, d.k, ldb,
-                       (uint32_t)std::min(128, plan->cta_n / plan->ctas_per_tile), "B");
+                       (uint32_t)(plan->cta_n > 256 ? 128 : plan->cta_n / plan->ctas_per_tile), "B");
   else                // storage k × n: [64 k × 64 n] boxes
     st = encode_f16_2d(&tbm, B, d.k, d.n, ldb, (uint32_t)plan->kb, "B");
   if (st != TB_OK) return st;
@@ -1390,8 +1391,10 @@ extern "C" tbStatus tb_device_status(void* stream, uint32_t* raw) {
   if (v != 0) {
     const uint32_t zero = 0;
     cudaMemcpyToSymbol(g_tb_status, &zero, sizeof(zero));
-    return tb_fail(TB_ERR_DEVICE_TIMEOUT, "a device-side wait timed out (status 0x" +
-                                              std::to_string(v) + ")");
+    char hex[16];
+    std::snprintf(hex, sizeof hex, "%08x", v);
+    return tb_fail(TB_ERR_DEVICE_TIMEOUT, std::string("a device-side wait timed out (status 0x") + hex +
+                                              ": code << 24 | site << 16 | block)");
   }
   return TB_OK;
 }

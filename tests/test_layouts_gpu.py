@@ -14,6 +14,8 @@ KNOBS = [
     ((256, 192, 320), dict(block_m=128, block_n=64, block_k=64)),
     ((512, 384, 256), dict(block_m=128, block_n=128, block_k=64, group_m=2)),
     ((1024, 1024, 512), dict(block_m=128, block_n=256, block_k=64)),
+    # one-CTA 128 × 256 hardware tile (group of 3 rows: no pairing)
+    ((640, 360, 512), dict(block_m=128, block_n=256, block_k=64, group_m=3, exact_tile=False)),
     ((1024, 1024, 512), dict(block_m=256, block_n=256, block_k=64, group_m=8)),
     ((1000, 744, 520), dict(block_m=256, block_n=128, block_k=64, exact_tile=False)),
     ((96, 80, 40), dict(block_m=64, block_n=64, block_k=16, exact_tile=False)),
