@@ -12,7 +12,7 @@ from conftest import make_inputs
 pytestmark = pytest.mark.gpu
 
 
-def _cases(count=120, seed=1234):
+def _cases(count=240, seed=1234):
     rng = np.random.default_rng(seed)
     out = []
     while len(out) < count:
