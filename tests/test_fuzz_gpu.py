@@ -62,9 +62,15 @@ def test_random_config_matches_oracle(cuda, case):
         Cin = Cin.astype(np.float16).astype(np.float32)
     bias = np.random.default_rng(m * n).standard_normal(n).astype(np.float32) if ex.get("bias") else None
     tC = torch.from_numpy(Cin.astype(np.float16) if out_dtype == "f16" else Cin).to(cuda)
-    tb.matmul(_view(A, a_col, cuda), _view(B, b_col, cuda), tC, beta=beta,
-              bias=None if bias is None else torch.from_numpy(bias).to(cuda),
-              activation=ex.get("activation"), **kn)
+    tA, tB = _view(A, a_col, cuda), _view(B, b_col, cuda)
+    tbias = None if bias is None else torch.from_numpy(bias).to(cuda)
+    if (m + n + k) % 3 == 0:
+        # every third case through a dynamic-shape plan (all dims open)
+        cfg = tb.KernelConfig(m=None, n=None, k=None, c_dtype=out_dtype, beta=beta, bias=bias is not None,
+                              activation=ex.get("activation"), a_col_major=a_col, b_col_major=b_col, **kn)
+        tb.DynamicMatmulPlan(cfg, cuda.index or 0).run(tA, tB, tC, bias=tbias)
+    else:
+        tb.matmul(tA, tB, tC, beta=beta, bias=tbias, activation=ex.get("activation"), **kn)
     torch.cuda.synchronize()
     assert tb.device_status() == 0
     want = oracle.apply_epilogue(oracle.matmul_ref(A, B, Cin if beta else None, beta=beta), bias,
