@@ -98,3 +98,9 @@ def test_kshard_nccl_rejects_bad_arguments_before_any_cuda_call():
     assert lib.tb_matmul_kshard_nccl_workspace_bytes(plan._h, 2, 520) == 512 * 512 * 4 + 256 * 512 * 4
     h = C.c_void_p()
     assert lib.tb_nccl_comm_create(3, 2, b"\0" * 128, C.byref(h)) == _capi.TB_ERR_INVALID_ARGUMENT
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """No CPU fallback: without the built library the bindings raise."""
+    with pytest.raises(ImportError, match="no CPU fallback"):
+        _capi.load(tmp_path / "libtbgemm.so")
