@@ -12,14 +12,15 @@ from conftest import make_inputs
 pytestmark = pytest.mark.gpu
 
 
-def _cases(count=240, seed=1234):
+def _cases(count=240, seed=1234, big=False):
     rng = np.random.default_rng(seed)
     out = []
     while len(out) < count:
         bm = int(rng.choice([64, 128, 256]))
         bn = int(rng.choice([64, 128, 256, 512]))
         bk = int(rng.choice([16, 32, 64]))
-        m, n, k = (int(x) for x in rng.integers(1, 700, 3))
+        hi = 3000 if big else 700
+        m, n, k = (int(x) for x in rng.integers(1, hi, 3))
         k = max(k, 16)
         kn = dict(block_m=bm, block_n=bn, block_k=bk, exact_tile=False, group_m=int(rng.integers(1, 9)))
         mode = rng.choice(["plain", "persistent", "serial", "parallel"])
@@ -37,7 +38,8 @@ def _cases(count=240, seed=1234):
     return out
 
 
-CASES = _cases()
+# many small cases, then fewer multi-wave ones (several tiles per CTA)
+CASES = _cases() + _cases(40, seed=777, big=True)
 
 
 def _view(x: np.ndarray, col_major: bool, dev):
