@@ -77,6 +77,9 @@ def _worker(rank, world, port, q, m, n, k, knobs):
     ((512, 384, 4096), dict(block_m=128, block_n=128, block_k=64)),
     # 256 × 200 rows per rank is not a whole number of 16 KB chunks: atomics path
     ((512, 200, 2048), dict(block_m=128, block_n=128, block_k=64, exact_tile=False)),
+    # ragged K slices, 1-CTA tiles, three split parts per rank
+    ((768, 264, 3000), dict(block_m=128, block_n=128, block_k=32, split_k=3,
+                            reduction_mode="split_k_parallel", exact_tile=False)),
 ])
 def test_two_rank_fused_kshard(cuda, shape, knobs):
     import torch
