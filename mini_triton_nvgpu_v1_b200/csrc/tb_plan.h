@@ -59,9 +59,10 @@ struct tb_matmul_plan {
   // Program pairing: two consecutive program ids whose tiles are adjacent in
   // the reference's launch order run as one hardware work item (same
   // programs, same results): 1 = vertical pair (grouped order, even group),
-  // 2 = horizontal pair (row-major / persistent order), 0 = none.
+  // 2 = horizontal pair (row-major / persistent order), 4 = 2 × 2 block
+  // (grouped order, even group and tile counts), 0 = none.
   int32_t fuse;
-  int64_t work_items;          // total_programs / (fuse ? 2 : 1)
+  int64_t work_items;          // total_programs / programs per item (1, 2 or 4)
   int32_t cta_m, cta_n;        // hardware tile (cta_m = 256: a CTA pair)
   int32_t ctas_per_tile;       // 1 or 2
   int32_t stages;              // shared-memory ring depth

@@ -170,12 +170,16 @@ def test_num_ctas_clamped_to_sms_and_programs():
 def test_program_pairing():
     """Two consecutive programs with adjacent tiles share a hardware tile when
     every pair in the launch order is aligned; the program set is unchanged."""
-    p = plan(4096, 4096, 4096, 128, 128, 64)                     # grouped, group 8
+    p = plan(2048, 2048, 4096, 128, 128, 64)                     # grouped, group 8
     assert p.info["fused_program_pairs"] == "vertical" and p.info["kernel"] == "tb_gemm_sm100_pair_256x128"
     assert p.info["work_items"] * 2 == p.total_programs
     for w in range(0, p.info["work_items"], 37):
         a, b = p.program_work(2 * w), p.program_work(2 * w + 1)
         assert a[0] % 2 == 0 and b[0] == a[0] + 1 and b[1] == a[1]          # vertical neighbours
+    # enough programs for every CTA pair: 2 × 2 blocks share a 256 × 256 pair tile
+    f = plan(4096, 4096, 4096, 128, 128, 64)
+    assert f.info["fused_program_pairs"] == "2x2" and f.info["kernel"] == "tb_gemm_sm100_pair_256x256"
+    assert f.info["work_items"] * 4 == f.total_programs
     q = plan(192, 128, 32, 64, 64, 32, persistent=True, num_ctas=2)          # row-major persistent
     assert q.info["fused_program_pairs"] == "horizontal"
     for w in range(q.info["work_items"]):

@@ -24,15 +24,29 @@ static int check(int tiles_m, int tiles_n, int group_m, int kind, int fuse) {
     a.programs_per_group = tiles_n;
   }
   a.total_programs = tiles_m * tiles_n;
-  const int items = fuse ? a.total_programs / 2 : a.total_programs;
+  const int items = fuse == 4 ? a.total_programs / 4 : fuse ? a.total_programs / 2 : a.total_programs;
   const int mode = walk_mode(a, fuse);
   std::vector<int> seen(a.total_programs, 0);
   for (int w = 0; w < items; ++w) {
     const int it = walk_item(a, fuse, mode, w);
     if (it < 0 || it >= items) return 1;
-    const int p0 = fuse ? 2 * it : it;
+    const int p0 = item_first_pid(a, fuse, it);
     const Work x = program_work(a, p0);
     ++seen[p0];
+    if (fuse == 4) {
+      const int rows = a.tiles_m - (x.tile_m / a.group_span_m) * a.group_span_m < a.group_span_m
+                           ? a.tiles_m - (x.tile_m / a.group_span_m) * a.group_span_m
+                           : a.group_span_m;
+      const int ps[3] = {p0 + 1, p0 + rows, p0 + rows + 1};
+      const int dm[3] = {1, 0, 1}, dn[3] = {0, 1, 1};
+      if (x.tile_m % 2 != 0 || x.tile_n % 2 != 0) return 5;
+      for (int j = 0; j < 3; ++j) {
+        const Work y = program_work(a, ps[j]);
+        ++seen[ps[j]];
+        if (y.tile_m != x.tile_m + dm[j] || y.tile_n != x.tile_n + dn[j]) return 6;
+      }
+      continue;
+    }
     if (fuse) {
       const Work y = program_work(a, p0 + 1);
       ++seen[p0 + 1];
@@ -57,7 +71,11 @@ int main() {
           printf("FAIL grouped-vertical %d %d %d: %d\n", tm, tn, g, r);
           return 1;
         }
-        cases += 2;
+        if (span % 2 == 0 && tm % 2 == 0 && tn % 2 == 0 && (r = check(tm, tn, g, kMapGroupedTile, 4))) {
+          printf("FAIL grouped-2x2 %d %d %d: %d\n", tm, tn, g, r);
+          return 1;
+        }
+        cases += 3;
       }
   for (int tm = 1; tm <= 30; ++tm)
     for (int tn = 1; tn <= 30; ++tn)
