@@ -229,7 +229,7 @@ __device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pid, 
   e.m0 = w.tile_m * p.block_m;
   e.n0 = w.tile_n * p.block_n;
   e.rows = min(p.block_m * (p.fuse == 1 || p.fuse == 4 ? 2 : 1), p.M - e.m0);
-  e.cols = min(p.block_n * (p.fuse == 2 || p.fuse == 4 ? 2 : 1), p.N - e.n0);
+  e.cols = min(p.block_n * (p.fuse >= 2 ? 2 : 1), p.N - e.n0);
   e.k_begin = w.kt_begin * p.block_k;
   e.k_end = min(p.K, (w.kt_begin + w.kt_count) * p.block_k);
   e.nkb = e.k_end > e.k_begin ? (e.k_end - e.k_begin + kb - 1) / kb : 0;
@@ -1205,7 +1205,7 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   memset(&tcm, 0, sizeof(tcm));
   kp.tma_out = kTmaNone;
   const bool exact_hw_tile = d.block_m * (plan->fuse == 1 || plan->fuse == 4 ? 2 : 1) == plan->cta_m &&
-                             d.block_n * (plan->fuse == 2 || plan->fuse == 4 ? 2 : 1) == plan->cta_n;
+                             d.block_n * (plan->fuse >= 2 ? 2 : 1) == plan->cta_n;
   if (exact_hw_tile && d.c_dtype == TB_F32 && aligned16(Cp) && ldc % 4 == 0) {
     if (plan->epilogue == kEpiStore) kp.tma_out = kTmaStoreC;
     if (plan->epilogue == kEpiAtomic) kp.tma_out = kTmaReduceC;

@@ -95,7 +95,7 @@ TB_HD int32_t walk_mode(const MappingArgs& a, int32_t fuse) {
 // Work item taken at position `w` of the walk.
 TB_HD int32_t walk_item(const MappingArgs& a, int32_t fuse, int32_t mode, int32_t w) {
   if (mode == kWalkSerpentine) {
-    const int32_t per = fuse == 1 ? 2 : fuse == 4 ? 4 : 1;  // programs per item
+    const int32_t per = fuse == 1 || fuse == 3 ? 2 : fuse == 4 ? 4 : 1;  // programs per item
     const int32_t ppg = a.programs_per_group / per;        // items per full group
     const int32_t g = w / ppg;
     if ((g & 1) == 0) return w;
@@ -103,7 +103,7 @@ TB_HD int32_t walk_item(const MappingArgs& a, int32_t fuse, int32_t mode, int32_
     const int32_t left = a.tiles_m - first;
     const int32_t rows = left < a.group_span_m ? left : a.group_span_m;
     const int32_t size = fuse == 1 || fuse == 4 ? rows / 2 : rows;  // items per item column
-    const int32_t ncols = fuse == 4 ? a.tiles_n / 2 : a.tiles_n;
+    const int32_t ncols = fuse == 3 || fuse == 4 ? a.tiles_n / 2 : a.tiles_n;
     const int32_t in = w - g * ppg;
     return g * ppg + (ncols - 1 - in / size) * size + in % size;
   }
@@ -121,17 +121,21 @@ TB_HD int32_t walk_item(const MappingArgs& a, int32_t fuse, int32_t mode, int32_
 
 // First program of work item `item`: fuse 1 = pids 2i, 2i+1 (vertical pair,
 // grouped order), 2 = pids 2i, 2i+1 (horizontal pair, row-major order),
-// 4 = a 2 × 2 block in grouped order: pids p, p + 1 (vertical pair in column
-// 2c) and p + rows, p + rows + 1 (the same pair in column 2c + 1), where rows
-// is the group's height (even). Items are numbered group by group, column
-// pair by column pair, down the rows, as the programs are.
+// 3 = pids p and p + rows (horizontal pair in grouped order: one row of a
+// group in columns 2c and 2c + 1, rows = the group's height), 4 = a 2 × 2
+// block in grouped order: pids p, p + 1 (vertical pair in column 2c) and
+// p + rows, p + rows + 1 (the same pair in column 2c + 1; rows even). Items
+// are numbered group by group, column pair by column pair, down the rows, as
+// the programs are.
 TB_HD int32_t item_first_pid(const MappingArgs& a, int32_t fuse, int32_t item) {
-  if (fuse != 4) return fuse ? 2 * item : item;
-  const int32_t group = (4 * item) / a.programs_per_group;
+  if (fuse != 3 && fuse != 4) return fuse ? 2 * item : item;
+  const int32_t per = fuse == 4 ? 4 : 2;
+  const int32_t group = (per * item) / a.programs_per_group;
   const int32_t first = group * a.group_span_m;
   const int32_t left = a.tiles_m - first;
   const int32_t rows = left < a.group_span_m ? left : a.group_span_m;
-  const int32_t wi = item - group * (a.programs_per_group / 4);
+  const int32_t wi = item - group * (a.programs_per_group / per);
+  if (fuse == 3) return group * a.programs_per_group + 2 * (wi / rows) * rows + wi % rows;
   const int32_t half = rows / 2;
   return group * a.programs_per_group + 2 * (wi / half) * rows + 2 * (wi % half);
 }

@@ -56,11 +56,12 @@ struct tb_matmul_plan {
 
   // --- this build's launch facts ---
   int32_t kernel_tile;         // TbKernelTile
-  // Program pairing: two consecutive program ids whose tiles are adjacent in
-  // the reference's launch order run as one hardware work item (same
-  // programs, same results): 1 = vertical pair (grouped order, even group),
-  // 2 = horizontal pair (row-major / persistent order), 4 = 2 × 2 block
-  // (grouped order, even group and tile counts), 0 = none.
+  // Program fusion: programs whose tiles are adjacent run as one hardware
+  // work item (same programs, same results; tb::item_first_pid): 1 =
+  // vertical pair (grouped order, even group),
+  // 2 = horizontal pair (row-major / persistent order), 3 = horizontal pair
+  // in grouped order (pids p and p + group rows), 4 = 2 × 2 block (grouped
+  // order, even group and tile counts), 0 = none.
   int32_t fuse;
   int64_t work_items;          // total_programs / programs per item (1, 2 or 4)
   int32_t cta_m, cta_n;        // hardware tile (cta_m = 256: a CTA pair)

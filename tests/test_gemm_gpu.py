@@ -85,6 +85,10 @@ CASES = [
                                                  exact_tile=False), "uniform", 17),
     ("fused_2x2_exact", (2304, 2304, 256), dict(block_m=128, block_n=128, block_k=64, group_m=4),
      "normal", 18),
+    ("fused_horizontal_ragged", (2200, 2300, 300), dict(block_m=256, block_n=128, block_k=64, group_m=8,
+                                                        exact_tile=False), "uniform", 19),
+    ("fused_horizontal_exact", (2304, 2304, 256), dict(block_m=256, block_n=128, block_k=64, group_m=3),
+     "normal", 20),
     ("pair256x512_grouped", (1024, 2048, 1024), dict(block_m=256, block_n=512, block_k=64, group_m=8),
      "normal", 4),
     ("pair256x512_ragged", (1000, 1300, 520), dict(block_m=256, block_n=512, block_k=64,

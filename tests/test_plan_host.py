@@ -180,6 +180,10 @@ def test_program_pairing():
     f = plan(4096, 4096, 4096, 128, 128, 64)
     assert f.info["fused_program_pairs"] == "2x2" and f.info["kernel"] == "tb_gemm_sm100_pair_256x256"
     assert f.info["work_items"] * 4 == f.total_programs
+    # 256 × 128 programs side by side in grouped order: one 256 × 256 pair tile
+    h = plan(4096, 4096, 4096, 256, 128, 64)
+    assert h.info["fused_program_pairs"] == "horizontal" and h.info["kernel"] == "tb_gemm_sm100_pair_256x256"
+    assert h.info["work_items"] * 2 == h.total_programs
     q = plan(192, 128, 32, 64, 64, 32, persistent=True, num_ctas=2)          # row-major persistent
     assert q.info["fused_program_pairs"] == "horizontal"
     for w in range(q.info["work_items"]):

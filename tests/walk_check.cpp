@@ -48,10 +48,16 @@ static int check(int tiles_m, int tiles_n, int group_m, int kind, int fuse) {
       continue;
     }
     if (fuse) {
-      const Work y = program_work(a, p0 + 1);
-      ++seen[p0 + 1];
+      int p1 = p0 + 1;
+      if (fuse == 3) {
+        const int first = (x.tile_m / a.group_span_m) * a.group_span_m;
+        const int left = a.tiles_m - first;
+        p1 = p0 + (left < a.group_span_m ? left : a.group_span_m);
+      }
+      const Work y = program_work(a, p1);
+      ++seen[p1];
       if (fuse == 1 && !(y.tile_m == x.tile_m + 1 && y.tile_n == x.tile_n)) return 2;
-      if (fuse == 2 && !(y.tile_n == x.tile_n + 1 && y.tile_m == x.tile_m)) return 3;
+      if (fuse >= 2 && !(y.tile_n == x.tile_n + 1 && y.tile_m == x.tile_m && x.tile_n % 2 == 0)) return 3;
     }
   }
   for (int v : seen)
@@ -69,6 +75,10 @@ int main() {
         const int span = g < tm ? g : tm;
         if (span % 2 == 0 && tm % 2 == 0 && (r = check(tm, tn, g, kMapGroupedTile, 1))) {
           printf("FAIL grouped-vertical %d %d %d: %d\n", tm, tn, g, r);
+          return 1;
+        }
+        if (tn % 2 == 0 && (r = check(tm, tn, g, kMapGroupedTile, 3))) {
+          printf("FAIL grouped-horizontal %d %d %d: %d\n", tm, tn, g, r);
           return 1;
         }
         if (span % 2 == 0 && tm % 2 == 0 && tn % 2 == 0 && (r = check(tm, tn, g, kMapGroupedTile, 4))) {
