@@ -204,8 +204,10 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": steps, "warmup": warm,
         "ms_per_step": round(1e3 * total_t / steps, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": f"tb.matmul {M}x{N_PER_GPU}x{K} f16->f32 (CPU sample per step)",
-                   "parallelism": "host threads"},
+        "config": {"workload": f"tb.matmul {M}x{N_PER_GPU * max(1, args.gpus)}x{K} f16->f32 C+=A·B, "
+                               f"N-sharded {N_PER_GPU} columns per GPU, GROUP_M=8",
+                   "m": M, "n_per_gpu": N_PER_GPU, "k": K, **{k: v for k, v in BLOCK.items()},
+                   "parallelism": f"host threads ({threads}); each step a {rows}-row sample"},
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
