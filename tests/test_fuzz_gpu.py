@@ -12,7 +12,7 @@ from conftest import make_inputs
 pytestmark = pytest.mark.gpu
 
 
-def _cases(count=240, seed=1234, big=False):
+def _cases(count=240, seed=1234, big=False, fusing=False):
     rng = np.random.default_rng(seed)
     out = []
     while len(out) < count:
@@ -21,9 +21,16 @@ def _cases(count=240, seed=1234, big=False):
         bk = int(rng.choice([16, 32, 64]))
         hi = 3000 if big else 700
         m, n, k = (int(x) for x in rng.integers(1, hi, 3))
+        if fusing:  # enough 128-class programs for the 2 × 2 / horizontal fusions
+            bm, bn = int(rng.choice([128, 256])), 128
+            # even tile counts (ragged last tiles) so both fusions can apply
+            m = 2 * bm * int(rng.integers(8, 15)) - int(rng.integers(0, bm))
+            n = 256 * int(rng.integers(8, 15)) - int(rng.integers(0, 128))
+            k = int(rng.integers(64, 600))
         k = max(k, 16)
-        kn = dict(block_m=bm, block_n=bn, block_k=bk, exact_tile=False, group_m=int(rng.integers(1, 9)))
-        mode = rng.choice(["plain", "persistent", "serial", "parallel"])
+        kn = dict(block_m=bm, block_n=bn, block_k=bk, exact_tile=False,
+                  group_m=int(rng.choice([2, 4, 6, 8])) if fusing else int(rng.integers(1, 9)))
+        mode = "plain" if fusing else rng.choice(["plain", "persistent", "serial", "parallel"])
         if mode == "persistent":
             kn.update(persistent=True, num_ctas=int(rng.integers(1, 200)))
         elif mode in ("serial", "parallel"):
@@ -39,7 +46,7 @@ def _cases(count=240, seed=1234, big=False):
 
 
 # many small cases, then fewer multi-wave ones (several tiles per CTA)
-CASES = _cases() + _cases(40, seed=777, big=True)
+CASES = _cases() + _cases(40, seed=777, big=True) + _cases(24, seed=4242, fusing=True)
 
 
 def _view(x: np.ndarray, col_major: bool, dev):
