@@ -3,19 +3,22 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-A step is one tb.matmul (C ← C_in + A·B, f16 A/B, f32 C) of the per-GPU
-problem 8192 × 8192 × 8192 with GROUP_M=8 program swizzle (the BASELINE
-"Grouped-M swizzle" config). With N GPUs the global problem is
-8192 × (8192·N) × 8192 sharded along N columns — each rank holds A and its
-own B/C column slice, no collective (weak scaling). Inputs are seeded
-synthetic N(0,1)·0.1 f16; A+B+C = 512 MiB per GPU, larger than the 126 MB L2,
+A step is one tb.matmul (C ← C_in + A·B, f16 A/B, f32 C) of the fixed
+8192 × 8192 × 8192 problem with GROUP_M=8 program swizzle (the BASELINE
+"Grouped-M swizzle" config). With N GPUs the same problem is sharded along
+N: rank r owns 8192/N columns of B and C (whole 256-column program tiles), A
+is replicated, no collective (strong scaling; `--scaling weak` gives every
+rank a full 8192-column slice instead). Inputs are seeded synthetic
+N(0,1)·0.1 f16; A+B+C exceed the 126 MB L2 at every N (A alone is 128 MiB),
 so no flush is needed between steps.
 
 JSON keys: value = whole-job TFLOP/s with inputs resident in HBM (CUDA
-events, max over ranks); e2e = the same through the public API with the
-step's inputs copied from pinned host memory and C copied back inside the
-timed region; roofline = the GEMM kernel's achieved TFLOP/s against the
-measured cuBLAS bf16 peak; cpu_baseline = the CPU oracle on the host cores.
+events, max over ranks); e2e = the same through the public API
+(parallel.NShard → tb_matmul_run_nshard) with the step's inputs copied from
+pinned host memory and C copied back inside the timed region; roofline = the
+GEMM kernel's achieved TFLOP/s against the measured cuBLAS bf16 peak (burst
+figure for a timed region under 0.5 s, sustained figure for longer ones);
+cpu_baseline = the CPU oracle on the host cores.
 
 --impl reference times the reference's CPU path for tb.matmul on the host
 cores: the reference itself cannot be built here (it is an MLIR dialect and
@@ -54,6 +57,9 @@ def parse():
     ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "splitk", "sweep"],
                     help="gemm8192: the headline 8192^3 N-sharded GEMM; splitk: the skinny "
                          "512x512x65536 split-K config (K-sharded + reduce-scatter at N>1)")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="gemm8192 at N>1: strong = the fixed 8192^3 problem split along N "
+                         "(BASELINE's config); weak = 8192 columns per GPU")
     ap.add_argument("--kshard", default="peer", choices=["peer", "capi", "nccl"],
                     help="splitk at N>1: reduce-scatter fused into the GEMM over NVLink (peer), "
                          "the C ABI's NCCL reduce-scatter run (capi), or torch.distributed's "
@@ -69,31 +75,48 @@ def peaks():
     return FALLBACK_PEAK_TFLOPS, 1400.0, "fallback"
 
 
-def traffic_for(kernel: str):
-    """DRAM bytes per launch of `kernel` on this workload, from the committed
-    ncu summary (profiles/traffic.json); None when not captured."""
+def traffic_for(kernel: str, n: int):
+    """DRAM bytes per launch of `kernel` on the M x n x K slice, from the
+    committed ncu summary (profiles/traffic.json); None when not captured."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None
     d = json.loads(p.read_text())
-    e = d.get(f"{kernel} {M}x{N_PER_GPU}x{K}")
+    e = d.get(f"{kernel} {M}x{n}x{K}")
     return None if e is None else e.get("dram_bytes_per_launch")
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons of one GPU, sampled every
-    200 ms while running."""
+    """SM clock, power and clock-event reasons of one GPU, polled through
+    NVML every ~2 ms while running (so a timed region of a few ms still gets
+    samples); nvidia-smi at 200 ms when NVML is unavailable."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ((0x8, "hw_slowdown"), (0x40, "hw_thermal_slowdown"), (0x20, "sw_thermal_slowdown"),
+               (0x4, "sw_power_cap"), (0x80, "hw_power_brake_slowdown"))
 
-    def __init__(self, phys_index: int):
+    def __init__(self, phys_index: int, period_s: float = 0.002):
         self.idx = phys_index
+        self.period = period_s
         self.rows = []
         self.proc = None
         self.t = None
+        self.stop_flag = threading.Event()
+        self.nvml = None
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
@@ -104,13 +127,41 @@ class ClockSampler:
         self.t = threading.Thread(target=self._read, daemon=True)
         self.t.start()
 
+    def _poll(self):
+        nv = self.nvml
+        while not self.stop_flag.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.rows.append((time.perf_counter(), sm, pw, rs))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
     def _read(self):
         for line in self.proc.stdout:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) >= 9:
                 self.rows.append(parts)
 
-    def stop(self):
+    def stop(self, window=None):
+        """Summary of the samples inside `window` (perf_counter start, end)
+        when given, else of all samples."""
+        if self.nvml is not None:
+            self.stop_flag.set()
+            if self.t:
+                self.t.join(timeout=2)
+            rows = [r for r in self.rows if window is None or window[0] <= r[0] <= window[1]]
+            if not rows:
+                rows = self.rows[-3:]
+            if not rows:
+                return None
+            reasons = sorted({name for r in rows for bit, name in self.REASONS if r[3] & bit})
+            return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(rows),
+                    "sm_mhz_min": min(r[1] for r in rows), "power_w_max": round(max(r[2] for r in rows), 1),
+                    "source": f"NVML every {self.period * 1e3:.0f} ms inside the timed region"}
         if self.proc is None:
             return None
         time.sleep(0.25)
@@ -128,7 +179,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(self.rows), "source": "nvidia-smi every 200 ms"}
 
 
 def phys_gpu_index(local: int) -> int:
@@ -199,15 +250,17 @@ def run_reference(args):
     value = total_f / total_t / 1e12
     sample = (f"{rows} of {M} rows of the {M}x{N_PER_GPU}x{K} tb.matmul per step (reference semantics "
               f"through oracle/tb_oracle.c; the MLIR reference needs an LLVM/MLIR toolchain absent here)")
+    n_glob = N_PER_GPU * max(1, args.gpus) if args.scaling == "weak" else N_PER_GPU
     out = {
         "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": steps, "warmup": warm,
-        "ms_per_step": round(1e3 * total_t / steps, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(1e3 * total_t / steps, 3), "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": f"tb.matmul {M}x{N_PER_GPU * max(1, args.gpus)}x{K} f16->f32 C+=A·B, "
-                               f"N-sharded {N_PER_GPU} columns per GPU, GROUP_M=8",
-                   "m": M, "n_per_gpu": N_PER_GPU, "k": K, **{k: v for k, v in BLOCK.items()},
-                   "parallelism": f"host threads ({threads}); each step a {rows}-row sample"},
+        "config": {"workload": f"tb.matmul {M}x{n_glob}x{K} f16->f32 C+=A·B, GROUP_M=8",
+                   "m": M, "n": n_glob, "k": K, **{k: v for k, v in BLOCK.items()},
+                   "rows_per_step": rows,
+                   "parallelism": f"host threads ({threads}); each step a {rows}-row sample of the "
+                                  f"{M}-row problem (a rate over the same per-row work)"},
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -217,11 +270,14 @@ def run_reference(args):
     return 0
 
 
+BURST_REGION_S = 0.5  # timed regions shorter than this are compared with the burst peak
+
+
 def run_ours(args):
-    import numpy as np
     import torch
     import torch.distributed as dist
     import mini_triton_nvgpu_v1_b200 as tb
+    from mini_triton_nvgpu_v1_b200 import parallel as par
 
     rank, world, local = dist_env()
     if world > 1:
@@ -230,21 +286,29 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream(dev)
 
-    # Per-rank shard: A replicated, B/C column slice `rank` of the global N.
+    # The whole problem is M x n_glob x K; rank r owns columns [col0, col0 +
+    # ncols) of B and C (tb_matmul_nshard_columns: whole 256-column tiles).
+    n_glob = N_PER_GPU * world if args.scaling == "weak" else N_PER_GPU
+    cfg = tb.KernelConfig(m=M, n=n_glob, k=K, **BLOCK)
+    shard = par.NShard(cfg, rank, world, local)
+    col0, ncols = shard.col0, shard.ncols
     g = torch.Generator(device=dev).manual_seed(4)
     A = (torch.randn(M, K, device=dev, generator=g) * 0.1).half()
-    g.manual_seed(1000 + rank)
-    B = (torch.randn(K, N_PER_GPU, device=dev, generator=g) * 0.1).half()
-    Cm = torch.zeros(M, N_PER_GPU, device=dev, dtype=torch.float32)
-
-    cfg = tb.KernelConfig(m=M, n=N_PER_GPU, k=K, **BLOCK)
-    plan = tb.MatmulPlan(cfg, local)
-    info = plan.info
+    # B's column slice, generated in 1024-column blocks of the seeded global B
+    B = torch.empty(K, ncols, device=dev, dtype=torch.float16)
+    for c in range(0, ncols, 1024):
+        g.manual_seed(1000 + (col0 + c) // 1024)
+        w = min(1024, ncols - c)
+        B[:, c:c + w] = (torch.randn(K, 1024, device=dev, generator=g) * 0.1).half()[:, :w]
+    Cm = torch.zeros(M, ncols, device=dev, dtype=torch.float32)
+    ws = torch.empty(max(1, shard.workspace_bytes), dtype=torch.uint8, device=dev)
+    local_plan = tb.MatmulPlan(tb.KernelConfig(m=M, n=ncols, k=K, **BLOCK), local)
+    info = local_plan.info
     launches_per_step = 1 + (1 if info["epilogue"] == "workspace_partial" else 0)
 
     def step():
-        plan.run_ptr(A.data_ptr(), K, B.data_ptr(), N_PER_GPU, Cm.data_ptr(), N_PER_GPU, 0, 0,
-                     stream.cuda_stream)
+        shard.run_ptr(A.data_ptr(), K, B.data_ptr(), ncols, Cm.data_ptr(), ncols, ws.data_ptr(),
+                      shard.workspace_bytes, stream.cuda_stream)
 
     def barrier():
         if world > 1:
@@ -258,23 +322,26 @@ def run_ours(args):
 
     sampler = ClockSampler(phys_gpu_index(local))
     sampler.start()
-    time.sleep(0.3)
+    time.sleep(0.05)
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start = time.perf_counter()
     ev0.record(stream)
     for _ in range(args.steps):
         step()
     ev1.record(stream)
     barrier()
-    clocks = sampler.stop()
+    t_end = time.perf_counter()
+    clocks = sampler.stop((t_start, t_end))
     ms = ev0.elapsed_time(ev1)
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     ms_step = ms_max / args.steps
-    flops_step_rank = 2.0 * M * N_PER_GPU * K
-    value = flops_step_rank * world / (ms_step * 1e-3) / 1e12
+    flops_step = 2.0 * M * n_glob * K          # whole job
+    flops_rank = 2.0 * M * ncols * K
+    value = flops_step / (ms_step * 1e-3) / 1e12
     tb.device_status(stream)
 
     # ---- e2e: public API, inputs from pinned host memory, result read back ----
@@ -284,8 +351,8 @@ def run_ours(args):
     # PCIe direction) overlap the GEMM of the compute stream.
     hA = A.cpu().pin_memory()
     hB = B.cpu().pin_memory()
-    hC = torch.zeros(M, N_PER_GPU, dtype=torch.float32).pin_memory()
-    hOut = [torch.empty(M, N_PER_GPU, dtype=torch.float32).pin_memory() for _ in range(2)]
+    hC = torch.zeros(M, ncols, dtype=torch.float32).pin_memory()
+    hOut = [torch.empty(M, ncols, dtype=torch.float32).pin_memory() for _ in range(2)]
     bufs = [(torch.empty_like(A), torch.empty_like(B), torch.empty_like(Cm)) for _ in range(2)]
     up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev = lambda: torch.cuda.Event()
@@ -303,7 +370,7 @@ def run_ours(args):
             uploaded = ev()
             uploaded.record(up)
         stream.wait_event(uploaded)
-        tb.matmul(dA, dB, dC, stream=stream, **BLOCK)
+        shard.run(dA, dB, dC, workspace=ws, stream=stream)
         computed = ev()
         computed.record(stream)
         with torch.cuda.stream(down):
@@ -327,41 +394,56 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.item()) / args.e2e_steps
-    e2e_value = flops_step_rank * world / (e2e_ms * 1e-3) / 1e12
-    h2d = A.numel() * 2 + B.numel() * 2 + Cm.numel() * 4
-    d2h = Cm.numel() * 4
+    e2e_value = flops_step / (e2e_ms * 1e-3) / 1e12
+    # whole-job bytes per step: every rank uploads A, its B and C_in slices
+    # and downloads its C slice
+    h2d = torch.tensor([A.numel() * 2 + B.numel() * 2 + Cm.numel() * 4], device=dev, dtype=torch.float64)
+    d2h = torch.tensor([Cm.numel() * 4], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(h2d)
+        dist.all_reduce(d2h)
 
     if rank == 0:
         peak, peak_sus, peak_src = peaks()
-        achieved = flops_step_rank / (ms_step * 1e-3) / 1e12  # one launch per step on this config
+        achieved = flops_rank / (ms_step * 1e-3) / 1e12  # rank 0's kernel: one launch per step
+        region_s = ms_max * 1e-3
+        burst = region_s < BURST_REGION_S or peak_sus is None
+        denom = peak if burst else peak_sus
         kern = info["kernel"]
         cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline_block()
+        alg_bytes = 2 * (M * K + K * ncols) + 8 * M * ncols
+        traffic = traffic_for(kern, ncols)
+        strong = args.scaling == "strong"
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f16",
             "data": "synthetic",
-            "config": {"workload": f"tb.matmul {M}x{N_PER_GPU * world}x{K} f16->f32 C+=A·B, "
-                                   f"N-sharded {N_PER_GPU} columns per GPU, GROUP_M=8",
-                       "m": M, "n_per_gpu": N_PER_GPU, "k": K, **{k: v for k, v in BLOCK.items()},
+            "config": {"workload": f"tb.matmul {M}x{n_glob}x{K} f16->f32 C+=A·B, N-sharded "
+                                   f"{'into ' + str(world) + ' column slices' if strong else str(N_PER_GPU) + ' columns per GPU'}, GROUP_M=8",
+                       "m": M, "n": n_glob, "k": K, "n_per_gpu": ncols, **{k: v for k, v in BLOCK.items()},
                        "kernel": kern, "grid": info["grid"], "stages": info["stages"],
-                       "l2": "inputs larger than L2 (512 MiB per GPU), no flush",
-                       "parallelism": f"N-shard x{world}, no collective"},
-            "pct_of_peak": round(100.0 * value / world / peak, 2),
-            "pct_of_peak_note": "of the measured cuBLAS bf16 burst peak per GPU",
-            # The timed region is ~1 s of back-to-back launches under the
-            # 1 kW power cap, so the sustained cuBLAS figure is the denominator.
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_sus,
-                         "unit": "TFLOP/s", "frac": round(achieved / peak_sus, 4),
-                         "peak_source": f"{peak_src} cuBLAS bf16 sustained (MEASURED_PEAKS.json)",
+                       "tail_split": info["tail_split"],
+                       "l2": "inputs larger than L2 (A alone 128 MiB), no flush",
+                       "parallelism": f"N-shard x{world} through tb_matmul_run_nshard, no collective"},
+            "pct_of_peak": round(100.0 * achieved / peak, 2),
+            "pct_of_peak_note": "rank 0's kernel TFLOP/s over the measured cuBLAS bf16 burst peak per GPU",
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": denom,
+                         "unit": "TFLOP/s", "frac": round(achieved / denom, 4),
+                         "peak_source": f"{peak_src} cuBLAS bf16 {'burst' if burst else 'sustained'} "
+                                        f"(MEASURED_PEAKS.json): the timed region lasted {region_s:.3f} s "
+                                        f"({'<' if burst else '>='} {BURST_REGION_S} s)",
+                         "timed_region_s": round(region_s, 4),
                          "frac_of_burst": round(achieved / peak, 4),
-                         "traffic": traffic_for(kern),
-                         "algorithmic_bytes": 2 * (M * K + K * N_PER_GPU) + 8 * M * N_PER_GPU},
+                         "frac_of_sustained": None if peak_sus is None else round(achieved / peak_sus, 4),
+                         "traffic": traffic, "algorithmic_bytes": alg_bytes,
+                         "traffic_over_algorithmic": None if traffic is None else round(traffic / alg_bytes, 3)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 3),
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "mini_triton_nvgpu_v1_b200.matmul",
-                    "note": "steps pipelined over two buffer sets: upload, GEMM and download overlap"},
+                    "h2d_bytes_per_step": int(h2d.item()), "d2h_bytes_per_step": int(d2h.item()),
+                    "api": "mini_triton_nvgpu_v1_b200.parallel.NShard.run (tb_matmul_run_nshard)",
+                    "note": "whole-job bytes; steps pipelined over two buffer sets: upload, GEMM and "
+                            "download overlap"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }

@@ -92,6 +92,12 @@ typedef struct tb_matmul_desc {
    * a_col_major: A is m × k column-major, lda >= m (A^T row-major);
    * b_col_major: B is k × n column-major, ldb >= k (B^T row-major). */
   int32_t a_col_major, b_col_major;
+  /* 1: bitwise-repeatable runs. By default (0) a plain f32-output plan whose
+   * work items leave the last wave of SMs partly idle cuts its last items
+   * into K pieces that other SMs compute and reduce-add into C (results
+   * within the f32 tolerance, summation order not fixed). No counterpart in
+   * the reference. */
+  int32_t deterministic;
 } tb_matmul_desc;
 
 /* An open ("?") problem dim, for tb_matmul_plan_create_dynamic; the value
@@ -178,13 +184,41 @@ tbStatus tb_matmul_run(const tb_matmul_plan* plan, const void* A, int64_t lda,
  * TB_ERR_WORKSPACE without launching. No cudaMalloc/cudaFree or other
  * allocating routine is called. The first call on a device looks the array's
  * device address up (once per device); make that first call before any
- * stream capture. All calls share the one array: two calls whose kernels
+ * stream capture. The address is kept for the life of the process: after a
+ * cudaDeviceReset on that device it is stale, so do not call this entry
+ * point on a device that was reset. All calls share the one array: two calls whose kernels
  * overlap on the GPU (different streams, or different host threads) race on
  * it. Nothing in it needs to start at zero — each call writes every partial
  * before it reads it. */
 tbStatus tb_matmul_run_no_alloc(const tb_matmul_plan* plan, const void* A,
                                 int64_t lda, const void* B, int64_t ldb,
                                 void* C, int64_t ldc, void* stream);
+
+/* ---- N-column sharded runs (one process per GPU, no collective) ----
+ * The reference is single-GPU; its op splits along N with no exchange. For a
+ * plan of the whole m × n × k problem, rank r of `world` owns columns
+ * [col0, col0 + ncols) of B and C: whole block_n program tiles, balanced
+ * over the ranks. A is replicated. Each rank runs the op on its slice, a
+ * tb.matmul of m × ncols × k with the plan's knobs; every element gets the
+ * value the one-GPU run gives it (same program tile, same K order).
+ * Replaces, per rank, kernel_tb_kernel_0(A, B, C) on the rank's columns
+ * (LowerPipelineToNVGPU.cpp:2678-2711). */
+tbStatus tb_matmul_nshard_columns(const tb_matmul_plan* plan, int rank, int world,
+                                  int64_t* col0, int64_t* ncols);
+/* Workspace bytes of this rank's slice run (0 unless split_k_serial or a
+ * repacked operand needs some). */
+tbStatus tb_matmul_nshard_workspace_bytes(const tb_matmul_plan* plan, int rank,
+                                          int world, size_t* bytes);
+/* B_cols / C_cols address column col0 of B and C (row strides ldb, ldc):
+ * either this rank's own k × ncols and m × ncols slices, or B + col0 and
+ * C + col0 of full matrices. bias_cols: the slice's ncols bias values
+ * (NULL unless desc.bias). Row-major B only. A rank with no columns
+ * (world > column tiles) returns TB_OK without launching. */
+tbStatus tb_matmul_run_nshard(const tb_matmul_plan* plan, int rank, int world,
+                              const void* A, int64_t lda, const void* B_cols,
+                              int64_t ldb, void* C_cols, int64_t ldc,
+                              const float* bias_cols, void* workspace,
+                              size_t workspace_bytes, void* stream);
 
 /* ---- K-sharded runs over NVLink peer memory (one process per GPU) ----
  * The reference is single-GPU; its split-K reduction (ReductionPlan.cpp:137-192,
@@ -216,7 +250,10 @@ tbStatus tb_peer_barrier(tb_peer_comm* comm, void* stream);
 tbStatus tb_matmul_run_kshard_peer(const tb_matmul_plan* plan, tb_peer_comm* comm,
                                    const void* A, int64_t lda, const void* B,
                                    int64_t ldb, void* stream);
-/* Synchronises `stream`; TB_ERR_DEVICE_TIMEOUT if a barrier wait gave up. */
+/* Synchronises `stream`; TB_ERR_DEVICE_TIMEOUT if a barrier wait gave up.
+ * A timed-out comm is failed for good: its later barrier and scatter kernels
+ * return at once (so the other ranks time out too), and runs and barriers on
+ * it are refused; destroy it and create a new one. */
 tbStatus tb_peer_comm_status(tb_peer_comm* comm, void* stream, uint32_t* raw);
 tbStatus tb_peer_comm_destroy(tb_peer_comm* comm);
 

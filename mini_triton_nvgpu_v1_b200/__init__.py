@@ -103,6 +103,8 @@ class KernelConfig:
     # operand storage: column-major A (m × k, lda >= m) / B (k × n, ldb >= k)
     a_col_major: bool = False
     b_col_major: bool = False
+    # bitwise-repeatable runs: no K pieces reduce-added into C for tail balancing
+    deterministic: bool = False
 
     def to_desc(self) -> _capi.tb_matmul_desc:
         d = _capi.tb_matmul_desc()
@@ -133,6 +135,7 @@ class KernelConfig:
             d.clamp_lo, d.clamp_hi = float(self.clamp[0]), float(self.clamp[1])
         d.a_col_major = 1 if self.a_col_major else 0
         d.b_col_major = 1 if self.b_col_major else 0
+        d.deterministic = 1 if self.deterministic else 0
         return d
 
 
@@ -320,7 +323,8 @@ def matmul(A, B, Cm, *, block_m: int = 128, block_n: int = 256, block_k: int = 6
            group_m: int = 8, exact_tile: Optional[bool] = None, num_warps: int = 4,
            num_stages: int = 2, split_k: int = 1, reduction_mode: Optional[str] = None,
            persistent: bool = False, num_ctas: int = 1, beta: int = 1, workspace=None,
-           stream=None, bias=None, activation: Optional[str] = None, clamp=None):
+           stream=None, bias=None, activation: Optional[str] = None, clamp=None,
+           deterministic: bool = False):
     """``tb.matmul %A, %B, %C {…}``: C ← C + A·B in place (beta=1, the
     reference semantics) or C ← A·B (beta=0). A [m,k] f16, B [k,n] f16,
     C [m,n] f32 (or f16, this build's extension). Returns C.
@@ -328,14 +332,16 @@ def matmul(A, B, Cm, *, block_m: int = 128, block_n: int = 256, block_k: int = 6
     ``exact_tile=None`` picks True when the tile divides the problem.
     ``bias`` (f32, length n), ``activation`` ("relu" | "silu" | "gelu_tanh")
     and ``clamp`` ((lo, hi)) are fused epilogue expressions applied, in that
-    order, to the complete sum before the output conversion."""
+    order, to the complete sum before the output conversion.
+    ``deterministic=True`` keeps every tile's sum in one fixed order (no
+    tail-balancing K pieces), so repeated runs are bitwise equal."""
     import torch
     # Fast path: everything that decides the plan and the leading dimensions
     # is in the key, so a hit skips validation and plan construction.
     key = (A.shape, B.shape, Cm.shape, A.stride(), B.stride(), Cm.stride(), A.dtype, B.dtype,
            Cm.dtype, A.device, B.device, Cm.device, block_m, block_n, block_k, group_m, exact_tile,
            num_warps, num_stages, split_k, reduction_mode, persistent, num_ctas, beta,
-           bias is None, activation, None if clamp is None else tuple(clamp))
+           bias is None, activation, None if clamp is None else tuple(clamp), deterministic)
     hit = _FAST.get(key)
     if hit is None:
         m, k = A.shape
@@ -353,7 +359,7 @@ def matmul(A, B, Cm, *, block_m: int = 128, block_n: int = 256, block_k: int = 6
                            c_dtype="f16" if Cm.dtype == torch.float16 else "f32", beta=beta,
                            bias=bias is not None, activation=activation,
                            clamp=tuple(clamp) if clamp is not None else None,
-                           a_col_major=a_col, b_col_major=b_col)
+                           a_col_major=a_col, b_col_major=b_col, deterministic=deterministic)
         plan = plan_for(cfg, Cm.device.index if Cm.is_cuda else None)
         _check_tensors(cfg, A, B, Cm)
         # the bound C entry points and the device index ride along, so a hit

@@ -57,6 +57,7 @@ class tb_matmul_desc(C.Structure):
         ("clamp", C.c_int32),
         ("clamp_lo", C.c_float), ("clamp_hi", C.c_float),
         ("a_col_major", C.c_int32), ("b_col_major", C.c_int32),
+        ("deterministic", C.c_int32),
     ]
 
 
@@ -99,6 +100,12 @@ PROTOTYPES = {
                                            C.POINTER(C.c_void_p)]),
     "tb_matmul": (C.c_int, [C.POINTER(tb_matmul_desc), C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
                             C.c_void_p, C.c_int64, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "tb_matmul_nshard_columns": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int64),
+                                           C.POINTER(C.c_int64)]),
+    "tb_matmul_nshard_workspace_bytes": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_size_t)]),
+    "tb_matmul_run_nshard": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int64, C.c_void_p,
+                                       C.c_int64, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
+                                       C.c_size_t, C.c_void_p]),
     "tb_peer_comm_create": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
                                       C.POINTER(C.c_void_p), C.POINTER(tb_peer_handle)]),
     "tb_peer_comm_connect": (C.c_int, [C.c_void_p, C.POINTER(tb_peer_handle)]),

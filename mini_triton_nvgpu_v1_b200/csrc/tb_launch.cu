@@ -46,21 +46,6 @@ using namespace tb::sm100;
 
 __device__ uint32_t g_tb_status = 0;
 
-#ifdef TB_WAIT_PROFILE
-// Debug builds only: cycles each role spent in bounded waits, summed over CTAs.
-// [0] producer/empty [1] mma/full [2] mma/tempty [3] epilogue/tfull
-// [4] kernel cycles (per CTA, summed) [5] epilogue busy cycles
-__device__ unsigned long long g_tb_prof[8];
-#define TB_PROF_ADD(i, v) atomicAdd(&g_tb_prof[i], (unsigned long long)(v))
-// per-fill timestamps of CTA 0: [0] MMA commit issued, [1] producer saw
-// empty, [2] MMA saw full (fill index f = k-block count since start)
-__device__ long long g_tb_ts[3][512];
-#define TB_TS(which, f) do { if (blockIdx.x == 0 && (f) < 512) g_tb_ts[which][f] = clock64(); } while (0)
-#else
-#define TB_TS(which, f) ((void)0)
-#define TB_PROF_ADD(i, v) ((void)0)
-#endif
-
 namespace {
 
 constexpr int kThreads = 192;
@@ -104,11 +89,7 @@ struct Cfg {
   static constexpr uint32_t kEpiBufBytes = 32 * 32 * 4;
   static constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBufBytes;
   static constexpr int kRawStages = (int)((kSmemLimit - 1024 - 512 - kEpiBytes) / kStageBytes);
-#ifdef TB_DEBUG_MAX_STAGES
-  static constexpr int kCap = TB_DEBUG_MAX_STAGES;  // debug builds: ring-depth experiments
-#else
   static constexpr int kCap = 8;
-#endif
   static constexpr int kStages = kRawStages > kCap ? kCap : kRawStages;
   static constexpr uint32_t kTmemCols = kAccs * BN;  // kAccs accumulators of BN f32 columns
   static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + kEpiBytes + 512;
@@ -161,7 +142,13 @@ struct KParams {
   int32_t fuse;      // program pairing (plan.fuse): work item w runs programs 2w and 2w+1
   int32_t cin_smem;  // one work item per CTA: the epilogue stages C_in through the idle ring
   int32_t walk_grouped;  // tb::WalkMode: the order resident CTAs take work items in
-  int32_t work_items;
+  int32_t work_items;    // hardware work items (programs × sub-tiles, or fused programs)
+  int32_t positions;     // walk positions: dp_items + tail_items · tail_parts
+  int32_t sub_m, sub_n;  // hardware tiles per program along M / N (programs larger than a tile)
+  // Tail balancing (tb::TailSplit): walk positions [0, dp_items) run whole
+  // work items; the last tail_items items are each cut into tail_parts
+  // K pieces that are reduce-added into C.
+  int32_t dp_items, tail_items, tail_parts;
   EpiExprs ex;       // applied in kEpiStore (split_k_serial: in the reduction)
   int32_t a_mn;      // A stored M-major (column-major m × k): MN-major UMMA operand
   int32_t b_kmaj;    // B stored K-major (column-major k × n): K-major UMMA operand
@@ -191,49 +178,64 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
-// wait_bounded plus (debug builds) the cycles spent waiting, added to slot.
-__device__ __forceinline__ bool wait_prof(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          uint32_t site, int slot, long long& acc) {
-#ifdef TB_WAIT_PROFILE
-  const long long t0 = clock64();
-  const bool r = wait_bounded(bar, parity, abort_flag, site);
-  acc += clock64() - t0;
-  return r;
-#else
-  (void)slot; (void)acc;
-  return wait_bounded(bar, parity, abort_flag, site);
-#endif
-}
-
 // Lane 0 waits (bounded), the result is broadcast so the warp stays converged.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          uint32_t site, int lane, long long& acc) {
+                                          uint32_t site, int lane) {
   // Every lane probes first with the non-blocking test_wait: in the common
   // case (phase already complete) that is one probe, while a blocking
   // try_wait costs hundreds of cycles even on a completed phase (measured:
   // 142 → 118 cycles per MMA for a 128×128 tile, 154 → 132 for 128×256).
   if (mbar_test_wait(bar, parity)) return true;
   int ok = 0;
-  if (lane == 0) ok = wait_prof(bar, parity, abort_flag, site, 0, acc);
+  if (lane == 0) ok = wait_bounded(bar, parity, abort_flag, site);
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
 struct Extent {
   int32_t m0, n0, rows, cols, k_begin, k_end, nkb, part;
+  bool piece;  // a K piece of a tail work item: its partial sum is reduce-added into C
 };
 
-__device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pid, int32_t kb) {
-  const int32_t item = tb::walk_item(p.map, p.fuse, p.walk_grouped, pid);
-  const tb::Work w = tb::program_work(p.map, tb::item_first_pid(p.map, p.fuse, item));
+// Work of walk position `pos` on a HM × HN hardware tile: its rows and
+// columns inside the problem (clipped to its program tile) and its K range;
+// nkb counts ring fills of kb K elements.
+template <int HM, int HN>
+__device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pos, int32_t kb) {
+  int32_t w = pos;
+  int32_t piece = -1;
+  if (pos >= p.dp_items) {
+    const int32_t t = pos - p.dp_items;
+    piece = t / p.tail_items;
+    w = p.dp_items + t % p.tail_items;
+  }
+  const int32_t nsub = p.sub_m * p.sub_n;
+  const int32_t sub = w % nsub;
+  const int32_t item = tb::walk_item(p.map, p.fuse, p.walk_grouped, w / nsub);
+  const tb::Work wk = tb::program_work(p.map, tb::item_first_pid(p.map, p.fuse, item));
   Extent e;
-  e.m0 = w.tile_m * p.block_m;
-  e.n0 = w.tile_n * p.block_n;
-  e.rows = min(p.block_m * (p.fuse == 1 || p.fuse == 4 ? 2 : 1), p.M - e.m0);
-  e.cols = min(p.block_n * (p.fuse >= 2 ? 2 : 1), p.N - e.n0);
-  e.k_begin = w.kt_begin * p.block_k;
-  e.k_end = min(p.K, (w.kt_begin + w.kt_count) * p.block_k);
-  e.nkb = e.k_end > e.k_begin ? (e.k_end - e.k_begin + kb - 1) / kb : 0;
-  e.part = w.part;
+  // A program larger than the hardware tile runs as sub_m × sub_n work
+  // items, each [HM × HN] of the program tile (the last ones clipped to it).
+  const int32_t sm = (sub / p.sub_n) * HM, sn = (sub % p.sub_n) * HN;
+  e.m0 = wk.tile_m * p.block_m + sm;
+  e.n0 = wk.tile_n * p.block_n + sn;
+  e.rows = min(p.block_m * (p.fuse == 1 || p.fuse == 4 ? 2 : 1) - sm, p.M - e.m0);
+  e.cols = min(p.block_n * (p.fuse >= 2 ? 2 : 1) - sn, p.N - e.n0);
+  if (nsub > 1) {
+    e.rows = min(e.rows, HM);
+    e.cols = min(e.cols, HN);
+  }
+  e.k_begin = wk.kt_begin * p.block_k;
+  e.k_end = min(p.K, (wk.kt_begin + wk.kt_count) * p.block_k);
+  e.nkb = e.k_end > e.k_begin && e.rows > 0 && e.cols > 0 ? (e.k_end - e.k_begin + kb - 1) / kb : 0;
+  e.part = wk.part;
+  e.piece = piece >= 0;
+  if (piece >= 0) {
+    const int32_t f0 = (int32_t)((int64_t)e.nkb * piece / p.tail_parts);
+    const int32_t f1 = (int32_t)((int64_t)e.nkb * (piece + 1) / p.tail_parts);
+    e.k_end = min(e.k_end, e.k_begin + f1 * kb);
+    e.k_begin += f0 * kb;
+    e.nkb = f1 - f0;
+  }
   return e;
 }
 
@@ -333,9 +335,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
-#ifdef TB_WAIT_PROFILE
-  const long long kernel_t0 = clock64();
-#endif
   const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
   const int lane = threadIdx.x % 32;
   const uint32_t rank = (G == 2) ? cluster_ctarank() : 0u;
@@ -378,28 +377,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     long long issued = 0;
-    long long prof_w = 0;
-    for (int32_t pid = first_pid; pid < p.work_items; pid += pid_stride) {
-      const Extent e = program_extent(p, pid, Cf::kKB);
+    for (int32_t pid = first_pid; pid < p.positions; pid += pid_stride) {
+      const Extent e = program_extent<kCtaM * G, BN>(p, pid, Cf::kKB);
       bool ok = true;
       for (int kb = 0; kb < e.nkb; ++kb) {
-        if (!warp_wait(smem_addr(&empty[stage]), phase ^ 1u, abort_flag, kSiteProducer, lane, prof_w)) {
+        if (!warp_wait(smem_addr(&empty[stage]), phase ^ 1u, abort_flag, kSiteProducer, lane)) {
           ok = false;
           break;
         }
-        if (lane == 0) TB_TS(1, issued);
         const uint32_t fb_local = smem_addr(&full[stage]);
-#ifdef TB_DEBUG_NO_LOADS
-        // Debug builds only: measure the MMA issue rate without operand traffic.
-        if (leader && elect_one()) mbar_arrive(fb_local);
-        __syncwarp();
-        ++issued;
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
-        }
-        continue;
-#endif
         const int kc = k_chunk(pid, first_pid, pid_stride, kb, e.nkb);
         const int32_t kx = e.k_begin + kc * Cf::kKB;
         const uint32_t dA = smem_addr(sA + (size_t)stage * Cf::kABytes);
@@ -470,7 +456,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
     }
     if (lane == 0) {
-      TB_PROF_ADD(0, prof_w);
       // Drain: the newest fill of each stage must land before the CTA exits
       // (only the leader's full barriers count the bytes).
       if (leader) {
@@ -515,13 +500,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t acc_phase = 0;
       bool issued_any = false;
       bool ok = true;
-      long long prof_full = 0, prof_te = 0;
-#ifdef TB_WAIT_PROFILE
-      long long mma_fills = 0;
-#endif
-      for (int32_t pid = first_pid; pid < p.work_items && ok; pid += pid_stride) {
-        const Extent e = program_extent(p, pid, Cf::kKB);
-        if (!warp_wait(smem_addr(&tempty[acc]), acc_phase ^ 1u, abort_flag, kSiteMma, lane, prof_te)) break;
+      for (int32_t pid = first_pid; pid < p.positions && ok; pid += pid_stride) {
+        const Extent e = program_extent<kCtaM * G, BN>(p, pid, Cf::kKB);
+        if (!warp_wait(smem_addr(&tempty[acc]), acc_phase ^ 1u, abort_flag, kSiteMma, lane)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         if (e.nkb == 0) {
@@ -532,11 +513,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
         } else {
           for (int kb = 0; kb < e.nkb; ++kb) {
-            if (!warp_wait(smem_addr(&full[stage]), phase, abort_flag, kSiteMma, lane, prof_full)) {
+            if (!warp_wait(smem_addr(&full[stage]), phase, abort_flag, kSiteMma, lane)) {
               ok = false;
               break;
             }
-            if (lane == 0) TB_TS(2, mma_fills);
             tc_fence_after();
             const int kc = k_chunk(pid, first_pid, pid_stride, kb, e.nkb);
             const int kvalid = min(Cf::kKB, e.k_end - (e.k_begin + kc * Cf::kKB));
@@ -578,13 +558,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               if constexpr (G == 2) umma_commit_pair(smem_addr(&empty[stage]), 0x3);
               else umma_commit(smem_addr(&empty[stage]));
-              TB_TS(0, mma_fills);
             }
             __syncwarp();
             issued_any = true;
-#ifdef TB_WAIT_PROFILE
-            ++mma_fills;
-#endif
             if (++stage == S) {
               stage = 0;
               phase ^= 1u;
@@ -601,10 +577,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc = 0;
           acc_phase ^= 1u;
         }
-      }
-      if (lane == 0) {
-        TB_PROF_ADD(1, prof_full);
-        TB_PROF_ADD(2, prof_te);
       }
       if (!ok && issued_any && lane == 0) {
         // Aborted with MMAs possibly in flight: wait for them before TMEM goes.
@@ -629,16 +601,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tempty_leader0 = G == 2 ? map_to_cta(smem_addr(&tempty[0]), 0) : smem_addr(&tempty[0]);
     int acc = 0;
     uint32_t acc_phase = 0;
-    long long prof_tf = 0;
-    for (int32_t pid = first_pid; pid < p.work_items; pid += pid_stride) {
-      const Extent e = program_extent(p, pid, Cf::kKB);
+    for (int32_t pid = first_pid; pid < p.positions; pid += pid_stride) {
+      const Extent e = program_extent<kCtaM * G, BN>(p, pid, Cf::kKB);
       int ok = 0;
-      if (lane == 0) ok = wait_prof(smem_addr(&tfull[acc]), acc_phase, abort_flag, kSiteEpilogue, 3, prof_tf);
+      if (lane == 0) ok = wait_bounded(smem_addr(&tfull[acc]), acc_phase, abort_flag, kSiteEpilogue);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
       const bool row_ok = row_in_tile < e.rows;
       const int64_t grow = (int64_t)e.m0 + row_in_tile;
+      // A K piece of a tail item adds its partial sum into C (which holds
+      // C_in and the other pieces' sums) instead of storing C_in + sum.
+      const int32_t tma_out = e.piece ? (int32_t)kTmaReduceC : p.tma_out;
       // When each CTA has a single work item, the mainloop's ring is idle
       // once tfull arrives (every MMA that read it has completed, and no
       // load follows). Each thread then copies its whole C_in row into it
@@ -684,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           return;
         }
         const OutT* src = reinterpret_cast<const OutT*>(p.C) + grow * p.ldc + e.n0 + c0;
-        if (ncol == 32 && (p.vec_c || p.tma_out == kTmaStoreC)) {
+        if (ncol == 32 && (p.vec_c || tma_out == kTmaStoreC)) {
           OutIO<OutT>::load32(src, c);
         } else {
 #pragma unroll
@@ -701,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int ncol = min(32, e.cols - c0);
         const int64_t gcol = (int64_t)e.n0 + c0;
-        if (p.tma_out != kTmaNone) {
+        if (tma_out != kTmaNone) {
           // TMA path (program tile == hardware tile). Stage [32 rows × 32
           // cols] in 128-byte-swizzled shared memory (row r's 16-byte chunk j
           // at chunk j ^ (r % 8): the warp's float4 writes are bank-conflict
@@ -711,13 +685,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.f;
           }
-          if (p.tma_out == kTmaStoreC && p.beta && row_ok) {
+          if (tma_out == kTmaStoreC && p.beta && row_ok) {
             float c[32];
             load_cin(c0, ncol, c);
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] += c[i];
           }
-          if (p.tma_out == kTmaStoreC && p.ex.any) {
+          if (tma_out == kTmaStoreC && p.ex.any) {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
               if (i < ncol) v[i] = apply_exprs(p.ex, v[i], gcol + i);
@@ -735,8 +709,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) {
             const int32_t y = (int32_t)(grow - lane);
-            if (p.tma_out == kTmaStoreC) tma_store_2d(&tmC, smem_addr(buf), (int32_t)gcol, y);
-            else if (p.tma_out == kTmaReduceC) tma_reduce_add_2d(&tmC, smem_addr(buf), (int32_t)gcol, y);
+            if (tma_out == kTmaStoreC) tma_store_2d(&tmC, smem_addr(buf), (int32_t)gcol, y);
+            else if (tma_out == kTmaReduceC) tma_reduce_add_2d(&tmC, smem_addr(buf), (int32_t)gcol, y);
             else tma_store_3d(&tmC, smem_addr(buf), (int32_t)gcol, y, e.part);
             bulk_commit_group();
           }
@@ -803,7 +777,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1u;
       }
     }
-    if (lane == 0 && q == 0) TB_PROF_ADD(3, prof_tf);
     // Outstanding TMA stores must finish before the CTA (and its shared
     // memory) goes away.
     if (lane == 0) bulk_wait_group<0>();
@@ -811,9 +784,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncthreads();
-#ifdef TB_WAIT_PROFILE
-  if (threadIdx.x == 0) TB_PROF_ADD(4, clock64() - kernel_t0);
-#endif
   if constexpr (G == 2) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
@@ -1176,6 +1146,12 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   kp.fuse = plan->fuse;
   kp.walk_grouped = tb::walk_mode(kp.map, plan->fuse);
   kp.work_items = (int32_t)plan->work_items;
+  kp.sub_m = plan->sub_m;
+  kp.sub_n = plan->sub_n;
+  kp.dp_items = (int32_t)plan->dp_items;
+  kp.tail_items = (int32_t)plan->tail_items;
+  kp.tail_parts = (int32_t)plan->tail_parts;
+  kp.positions = (int32_t)plan->positions;
   kp.a_mn = d.a_col_major ? 1 : 0;
   kp.b_kmaj = d.b_col_major ? 1 : 0;
   kp.ex.bias = d.bias ? bias : nullptr;
@@ -1187,7 +1163,7 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   kp.vec_c = aligned16(Cp) && ((ldc * (int64_t)out_bytes) % 16 == 0) &&
              ((d.block_n * (int64_t)out_bytes) % 16 == 0);
   kp.vec_ws = (d.n % 4 == 0) && (d.block_n % 4 == 0) && aligned16(workspace);
-  kp.cin_smem = plan->work_items <= plan->grid / plan->ctas_per_tile && kp.vec_c;
+  kp.cin_smem = plan->positions <= plan->grid / plan->ctas_per_tile && kp.vec_c;
   kp.C = Cp;
   kp.ldc = ldc;
   kp.ws = reinterpret_cast<float*>(workspace);
@@ -1204,14 +1180,23 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   CUtensorMap tcm;
   memset(&tcm, 0, sizeof(tcm));
   kp.tma_out = kTmaNone;
-  const bool exact_hw_tile = d.block_m * (plan->fuse == 1 || plan->fuse == 4 ? 2 : 1) == plan->cta_m &&
-                             d.block_n * (plan->fuse >= 2 ? 2 : 1) == plan->cta_n;
+  const bool exact_hw_tile =
+      d.block_m * (plan->fuse == 1 || plan->fuse == 4 ? 2 : 1) == (int64_t)plan->cta_m * plan->sub_m &&
+      d.block_n * (plan->fuse >= 2 ? 2 : 1) == (int64_t)plan->cta_n * plan->sub_n;
   if (exact_hw_tile && d.c_dtype == TB_F32 && aligned16(Cp) && ldc % 4 == 0) {
     if (plan->epilogue == kEpiStore) kp.tma_out = kTmaStoreC;
     if (plan->epilogue == kEpiAtomic) kp.tma_out = kTmaReduceC;
   }
   if (exact_hw_tile && plan->epilogue == kEpiWorkspace && aligned16(workspace) && d.n % 4 == 0)
     kp.tma_out = kTmaStoreWs;
+  // The tail's K pieces reduce-add f32 partial tiles through the same C
+  // tensor map; without it (C not TMA-addressable) every item runs whole.
+  if (plan->tail_items && kp.tma_out != kTmaStoreC) {
+    kp.dp_items = kp.work_items;
+    kp.tail_items = 0;
+    kp.tail_parts = 1;
+    kp.positions = kp.work_items;
+  }
   if (kp.tma_out != kTmaNone) {
     cuuint32_t box[3] = {32, 32, 1};
     CUresult r;
@@ -1272,20 +1257,6 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   }
   return TB_OK;
 }
-
-#ifdef TB_WAIT_PROFILE
-extern "C" int tb_debug_timestamps(long long* out) {
-  return cudaMemcpyFromSymbol(out, g_tb_ts, sizeof(g_tb_ts)) != cudaSuccess;
-}
-extern "C" int tb_debug_wait_profile(unsigned long long* out8, int reset) {
-  if (cudaMemcpyFromSymbol(out8, g_tb_prof, sizeof(unsigned long long) * 8) != cudaSuccess) return 1;
-  if (reset) {
-    unsigned long long z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    cudaMemcpyToSymbol(g_tb_prof, z, sizeof(z));
-  }
-  return 0;
-}
-#endif
 
 // ------------------------------------------------ allocation-free entry point
 //

@@ -44,6 +44,10 @@ struct FlagArgs {
 
 // thread s < world signals rank s; thread 0 then waits for its own flag.
 __global__ void tb_peer_barrier_kernel(FlagArgs a) {
+  // A comm whose earlier wait timed out is poisoned: the ranks' flag counts
+  // no longer agree, so a barrier could pass early. Do nothing; the ranks
+  // still waiting on this one time out and poison their comms in turn.
+  if (*(volatile unsigned int*)a.status != 0) return;
   const int t = threadIdx.x;
   if (t < a.world) {
     __threadfence_system();
@@ -95,6 +99,7 @@ __device__ __forceinline__ void wait_flag(const ScatterArgs& a, unsigned int tar
 }
 
 __global__ void __launch_bounds__(256) tb_peer_scatter_kernel(ScatterArgs a) {
+  if (*(volatile unsigned int*)a.status != 0) return;  // poisoned comm (see the barrier kernel)
   // Opening barrier: this rank's stream has reached the scatter, so its own
   // rows are free to receive; tell every rank, then wait until all ranks are.
   if (blockIdx.x == 0 && threadIdx.x == 0)
@@ -128,6 +133,9 @@ __global__ void __launch_bounds__(256) tb_peer_scatter_kernel(ScatterArgs a) {
             : "memory");
         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        // The bulk add ran in the async proxy: order it before this thread's
+        // generic-proxy flag and counter atomics that publish completion.
+        asm volatile("fence.proxy.async.global;" ::: "memory");
       }
       __syncthreads();
     }
@@ -174,6 +182,7 @@ struct tb_peer_comm {
   void* flag_opened[kMaxWorld];
   unsigned int phase;
   bool connected;
+  bool failed;  // a barrier wait timed out: the flag counts disagree, runs are refused
 };
 
 extern "C" tbStatus tb_peer_comm_create(int rank, int world, void* my_rows, int64_t rows_per_rank,
@@ -258,6 +267,8 @@ extern "C" tbStatus tb_peer_comm_connect(tb_peer_comm* c, const tb_peer_handle* 
 
 extern "C" tbStatus tb_peer_barrier(tb_peer_comm* c, void* stream) {
   if (!c || !c->connected) return tb_fail(TB_ERR_INVALID_ARGUMENT, "comm is not connected");
+  if (c->failed)
+    return tb_fail(TB_ERR_DEVICE_TIMEOUT, "this comm is failed: a peer barrier wait timed out earlier");
   FlagArgs a;
   std::memset(&a, 0, sizeof(a));
   for (int r = 0; r < c->world; ++r) a.flags[r] = c->flags[r];
@@ -277,6 +288,8 @@ extern "C" tbStatus tb_matmul_run_kshard_peer(const tb_matmul_plan* plan, tb_pee
   tb_clear_error();
   if (!plan || !c || !c->connected)
     return tb_fail(TB_ERR_INVALID_ARGUMENT, "plan and a connected comm are required");
+  if (c->failed)
+    return tb_fail(TB_ERR_DEVICE_TIMEOUT, "this comm is failed: a peer barrier wait timed out earlier");
   if (plan->dynamic)
     return tb_fail(TB_ERR_INVALID_ARGUMENT, "K-sharded runs take a plan with static dims");
   if (plan->desc.m != c->rows_per_rank * c->world || plan->desc.n != c->n)
@@ -345,7 +358,11 @@ extern "C" tbStatus tb_peer_comm_status(tb_peer_comm* c, void* stream, uint32_t*
   e = cudaMemcpy(&v, c->flag_base + 1, sizeof(v), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail("cudaMemcpy(status)", e);
   if (raw) *raw = v;
-  if (v) return tb_fail(TB_ERR_DEVICE_TIMEOUT, "a peer barrier wait timed out");
+  if (v) {
+    c->failed = true;
+    return tb_fail(TB_ERR_DEVICE_TIMEOUT,
+                   "a peer barrier wait timed out; this comm is failed (destroy it and build a new one)");
+  }
   return TB_OK;
 }
 

@@ -28,6 +28,7 @@ namespace {
 thread_local std::string g_last_error;
 
 constexpr int kDefaultB200Sms = 148;
+constexpr int64_t kMaxWarpsPerCta = 8;  // TargetInfo.cpp:126
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -70,6 +71,35 @@ bool derive_warp_grid(int64_t num_warps, int64_t bm, int64_t bn, int64_t* gm,
 
 }  // namespace
 
+void tb_choose_tail_split(int64_t items, int64_t slots, int64_t fills, int64_t* dp_items,
+                          int64_t* tail_items, int64_t* tail_parts) {
+  // Cost model in ring fills per slot (all items have `fills` fills): the
+  // whole waves before the tail keep their items whole; the remaining L
+  // items (one wave plus the partial one) are cut into s equal K pieces, each
+  // charged kPieceCost extra fills for its partial-tile reduce-add. A split is
+  // taken only when it shortens the modelled makespan by 3 % or more.
+  constexpr int64_t kPieceCost = 2;
+  *dp_items = items;
+  *tail_items = 0;
+  *tail_parts = 1;
+  if (slots <= 1 || items <= 0 || items % slots == 0 || fills < 16) return;
+  const int64_t whole = (items + slots - 1) / slots * fills;
+  int64_t best = whole - whole * 3 / 100;
+  const int64_t d = std::max<int64_t>(0, items / slots - 1) * slots;
+  const int64_t L = items - d;
+  for (int64_t s = 2; s <= 8 && fills / s >= 8; ++s) {
+    const int64_t pieces = L * s;
+    if (d + pieces > std::numeric_limits<int32_t>::max()) break;
+    const int64_t t = d / slots * fills + (pieces + slots - 1) / slots * ((fills + s - 1) / s + kPieceCost);
+    if (t < best) {
+      best = t;
+      *dp_items = d;
+      *tail_items = L;
+      *tail_parts = s;
+    }
+  }
+}
+
 tbStatus tb_fail(tbStatus code, const std::string& msg) {
   g_last_error = msg;
   return code;
@@ -104,6 +134,7 @@ extern "C" tbStatus tb_matmul_desc_init(tb_matmul_desc* d) {
   d->clamp_hi = 0.f;
   d->a_col_major = 0;
   d->b_col_major = 0;
+  d->deterministic = 0;
   return TB_OK;
 }
 
@@ -259,6 +290,10 @@ tbStatus tb_plan_build(const tb_matmul_desc& d, int device, int num_sms, tb_matm
     launch_groups = tiles_m;
     total = tiles_m * tiles_n;
   }
+  // ProgramMappingPlan.cpp:446-449: the target's limit is 8 warps per CTA
+  // (maxWarpsPerCTA, TargetInfo.cpp:126), checked whenever the SM count is known.
+  if (num_sms > 0 && d.num_warps > kMaxWarpsPerCta)
+    return tb_fail(TB_ERR_INVALID_ARGUMENT, "num_warps exceeds target max warps per CTA");
   if (d.persistent && num_ctas > num_sms) num_ctas = num_sms;  // :450-453
 
   if (total > std::numeric_limits<int32_t>::max() ||
@@ -294,21 +329,19 @@ tbStatus tb_plan_build(const tb_matmul_desc& d, int device, int num_sms, tb_matm
   else p.mainline_kind = "single_tile";
 
   // ---- this build's hardware tile: tcgen05 M=128 on one CTA, or M=256 on a
-  //      CTA pair (cta_group::2); N ∈ {64, 128, 256} ----
-  if (d.block_m > 256)
-    return tb_fail(TB_ERR_UNSUPPORTED,
-                   "block_m > 256 is not supported by the sm_100a kernels of this "
-                   "build (one tcgen05 accumulator of at most 256 rows per program)");
-  if (d.block_n > 512)
-    return tb_fail(TB_ERR_UNSUPPORTED,
-                   "block_n > 512 is not supported (two tcgen05 N = 256 accumulators fill TMEM)");
+  //      CTA pair (cta_group::2); N ∈ {64, 128, 256, 512} ----
+  // A program tile larger than every hardware tile (block_m > 256 or
+  // block_n > 512; KernelConfig.cpp:217-221 only asks for multiples of 16 /
+  // 8) runs as sub_m × sub_n hardware work items that together cover it;
+  // each computes its part of the program's tile over the program's K range.
+  const bool big = d.block_m > 256 || d.block_n > 512;
   // Consecutive program ids in grouped order are vertically adjacent tiles
   // (LowerPipelineToNVGPU.cpp:283-304: tile_m advances fastest inside a
   // group), and in row-major / persistent order horizontally adjacent. When
   // every such pair is aligned, two programs share one hardware tile (half
   // the operand traffic per FLOP); a 32-bit program walk stays the same.
   p.fuse = 0;
-  if (split_k == 1 && total % 2 == 0) {
+  if (!big && split_k == 1 && total % 2 == 0) {
     // 2 × 2 blocks of programs no larger than 128 × 128 make one 256 × 256
     // pair tile (measured 4096³ with 128 × 128 programs: 119 → 112 µs), when
     // every CTA pair still gets a work item.
@@ -330,9 +363,31 @@ tbStatus tb_plan_build(const tb_matmul_desc& d, int device, int num_sms, tb_matm
   p.work_items = p.fuse == 4 ? total / 4 : p.fuse ? total / 2 : total;
   const int64_t eff_bm = d.block_m * (p.fuse == 1 || p.fuse == 4 ? 2 : 1);
   const int64_t eff_bn = d.block_n * (p.fuse >= 2 ? 2 : 1);
-  // Pairing never builds a 256 × 512 tile: its single accumulator leaves the
-  // epilogue exposed (measured 5 % slower than 256 × 256 at 8192³).
-  if (eff_bn > 256) {  // 256 × 512 CTA pair (256 < block_n <= 512)
+  p.sub_m = p.sub_n = 1;
+  if (big) {
+    // Pair tiles for programs taller than 128 rows, else one-CTA 128-row
+    // tiles; the widest tile no wider than the program (256 × 512 only for
+    // programs at most 512 wide, where it covers the width in one item).
+    if (d.block_m > 128) {
+      p.cta_m = 256;
+      p.ctas_per_tile = 2;
+      if (d.block_n <= 128) { p.kernel_tile = kTile256x128; p.cta_n = 128; }
+      else if (d.block_n <= 256 || d.block_n > 512) { p.kernel_tile = kTile256x256; p.cta_n = 256; }
+      else { p.kernel_tile = kTile256x512; p.cta_n = 512; }
+    } else {
+      p.cta_m = 128;
+      p.ctas_per_tile = 1;
+      p.kernel_tile = kTile128x256;
+      p.cta_n = 256;
+    }
+    p.sub_m = (int32_t)ceil_div(d.block_m, p.cta_m);
+    p.sub_n = (int32_t)ceil_div(d.block_n, p.cta_n);
+    if (total * p.sub_m * p.sub_n > std::numeric_limits<int32_t>::max())
+      return tb_fail(TB_ERR_UNSUPPORTED, "hardware work items exceed 2^31-1");
+    p.work_items = total * p.sub_m * p.sub_n;
+  } else if (eff_bn > 256) {  // 256 × 512 CTA pair (256 < block_n <= 512)
+    // Pairing never builds a 256 × 512 tile: its single accumulator leaves
+    // the epilogue exposed (measured 5 % slower than 256 × 256 at 8192³).
     p.cta_m = 256;
     p.ctas_per_tile = 2;
     p.kernel_tile = kTile256x512;
@@ -398,9 +453,21 @@ tbStatus tb_plan_build(const tb_matmul_desc& d, int device, int num_sms, tb_matm
     else p.workspace_bytes = p.partial_bytes;
   }
   // Resident program slots: one per SM, or one per SM pair for CTA pairs.
-  const int64_t want = d.persistent ? std::min<int64_t>(p.resident_programs, p.work_items) : p.work_items;
   const int64_t slots = std::max<int64_t>(1, num_sms / p.ctas_per_tile);
-  p.grid = p.ctas_per_tile * std::max<int64_t>(1, std::min<int64_t>(want, slots));
+  const int64_t resident = d.persistent ? std::min<int64_t>(p.resident_programs, slots) : slots;
+  // Tail balancing: when the work items leave the last wave of resident
+  // slots partly idle (e.g. 128 items of 256 × 256 on 74 CTA pairs), the
+  // last items are cut into K pieces that fill the idle slots.
+  p.dp_items = p.work_items;
+  p.tail_items = 0;
+  p.tail_parts = 1;
+  const bool exact_hw = d.block_m * (p.fuse == 1 || p.fuse == 4 ? 2 : 1) == (int64_t)p.cta_m * p.sub_m &&
+                        d.block_n * (p.fuse >= 2 ? 2 : 1) == (int64_t)p.cta_n * p.sub_n;
+  if (!d.deterministic && split_k == 1 && d.c_dtype == TB_F32 && d.beta && !exprs && exact_hw)
+    tb_choose_tail_split(p.work_items, resident, ceil_div(d.k, p.kb), &p.dp_items, &p.tail_items,
+                         &p.tail_parts);
+  p.positions = p.dp_items + p.tail_items * p.tail_parts;
+  p.grid = p.ctas_per_tile * std::max<int64_t>(1, std::min<int64_t>(p.positions, resident));
 
   return TB_OK;
 }
@@ -485,6 +552,14 @@ extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* bu
         : plan->fuse == 4 ? "2x2" : "none")
     << "\", ";
   o << "\"work_items\": " << plan->work_items << ", ";
+  o << "\"program_subtiles\": [" << plan->sub_m << ", " << plan->sub_n << "], ";
+  o << "\"tail_split\": ";
+  if (plan->tail_items)
+    o << "{\"whole_items\": " << plan->dp_items << ", \"split_items\": " << plan->tail_items
+      << ", \"k_pieces\": " << plan->tail_parts << "}, ";
+  else
+    o << "null, ";
+  o << "\"walk_positions\": " << plan->positions << ", ";
   {
     const char* walks[] = {"program_order", "row_groups", "serpentine_groups"};
     o << "\"hardware_walk\": \"" << walks[tb::walk_mode(plan->map, plan->fuse)] << "\", ";

@@ -63,7 +63,12 @@ struct tb_matmul_plan {
   // in grouped order (pids p and p + group rows), 4 = 2 × 2 block (grouped
   // order, even group and tile counts), 0 = none.
   int32_t fuse;
-  int64_t work_items;          // total_programs / programs per item (1, 2 or 4)
+  int64_t work_items;          // total_programs / programs per item (1, 2 or 4), or × sub-tiles
+  int32_t sub_m, sub_n;        // hardware tiles per program along M / N (programs larger than a tile)
+  // Tail balancing (tb_choose_tail_split): walk positions [0, dp_items) run
+  // whole work items, the last tail_items items run as tail_parts K pieces
+  // each (reduce-added into C); positions = dp_items + tail_items·tail_parts.
+  int64_t dp_items, tail_items, tail_parts, positions;
   int32_t cta_m, cta_n;        // hardware tile (cta_m = 256: a CTA pair)
   int32_t ctas_per_tile;       // 1 or 2
   int32_t stages;              // shared-memory ring depth
@@ -94,6 +99,11 @@ tbStatus tb_plan_build(const tb_matmul_desc& d, int device, int num_sms, tb_matm
 
 // JSON facts of a dynamic plan; tb_dynamic.cpp.
 std::string tb_describe_dynamic(const tb_matmul_plan* plan);
+
+// Chooses the tail split for `items` equal work items of `fills` ring fills
+// on `slots` resident slots (tb_plan.cpp).
+void tb_choose_tail_split(int64_t items, int64_t slots, int64_t fills, int64_t* dp_items,
+                          int64_t* tail_items, int64_t* tail_parts);
 
 // Thread-local error message helpers (tb_plan.cpp).
 tbStatus tb_fail(tbStatus code, const std::string& msg);

@@ -67,6 +67,53 @@ def matmul_nshard(A, B_local, C_local, local_matmul: Optional[Callable] = None, 
     return f(A, B_local, C_local, **knobs)
 
 
+class NShard:
+    """N-column sharded tb.matmul through the C ABI (tb_matmul_run_nshard):
+    `cfg` describes the WHOLE m × n × k problem; rank `rank` of `world` runs
+    its columns [col0, col0 + ncols) (whole block_n tiles, balanced) with the
+    same knobs. No collective."""
+
+    def __init__(self, cfg, rank: int, world: int, device: Optional[int] = None):
+        import ctypes as C
+        from . import MatmulPlan, _check, _load_lib
+        self._lib = _load_lib()
+        self._check = _check
+        self.plan = MatmulPlan(cfg, device)
+        self.rank, self.world = rank, world
+        c0, nc = C.c_int64(0), C.c_int64(0)
+        _check(self._lib.tb_matmul_nshard_columns(self.plan._h, rank, world, C.byref(c0), C.byref(nc)))
+        self.col0, self.ncols = c0.value, nc.value
+        ws = C.c_size_t(0)
+        _check(self._lib.tb_matmul_nshard_workspace_bytes(self.plan._h, rank, world, C.byref(ws)))
+        self.workspace_bytes = ws.value
+
+    def run_ptr(self, a_ptr: int, lda: int, b_ptr: int, ldb: int, c_ptr: int, ldc: int,
+                ws_ptr: int = 0, ws_bytes: int = 0, stream: int = 0, bias_ptr: int = 0) -> None:
+        """b_ptr / c_ptr address column col0 of B and C (this rank's slices)."""
+        import ctypes as C
+        self._check(self._lib.tb_matmul_run_nshard(
+            self.plan._h, self.rank, self.world, C.c_void_p(a_ptr), lda, C.c_void_p(b_ptr), ldb,
+            C.c_void_p(c_ptr), ldc, C.c_void_p(bias_ptr or None), C.c_void_p(ws_ptr or None), ws_bytes,
+            C.c_void_p(stream or None)))
+
+    def run(self, A, B_cols, C_cols, workspace=None, stream=None, bias_cols=None) -> None:
+        """A [m, k]; B_cols [k, ncols] and C_cols [m, ncols]: this rank's
+        slices (or column views of full matrices), unit minor stride."""
+        import torch
+        if tuple(B_cols.shape) != (self.plan.cfg.k, self.ncols) or \
+                tuple(C_cols.shape) != (self.plan.cfg.m, self.ncols):
+            raise ValueError(f"rank {self.rank} owns {self.ncols} columns from {self.col0}")
+        ws_ptr, ws_bytes = 0, 0
+        if self.workspace_bytes:
+            if workspace is None:
+                workspace = torch.empty(self.workspace_bytes, dtype=torch.uint8, device=C_cols.device)
+            ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel()
+        s = stream if stream is not None else torch.cuda.current_stream(C_cols.device)
+        self.run_ptr(A.data_ptr(), A.stride(0), B_cols.data_ptr(), B_cols.stride(0), C_cols.data_ptr(),
+                     C_cols.stride(0), ws_ptr, ws_bytes, s.cuda_stream,
+                     0 if bias_cols is None else bias_cols.data_ptr())
+
+
 def matmul_kshard(A_local, B_local, C_rows, group=None, local_matmul: Optional[Callable] = None,
                   partial=None, **knobs):
     """K-sharded tb.matmul with a reduce-scatter.

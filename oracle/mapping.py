@@ -9,6 +9,9 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 
+MAX_WARPS_PER_CTA = 8  # maxWarpsPerCTA, lib/Analysis/TargetInfo.cpp:126
+
+
 def cdiv(a: int, b: int) -> int:
     return (a + b - 1) // b
 
@@ -76,7 +79,7 @@ class Mapping:
 
 
 def program_mapping(m, n, k, bm, bn, bk, group_m=8, split_k=1, persistent=False, num_ctas=1,
-                    reduction_mode=None, num_sms=148) -> Mapping:
+                    reduction_mode=None, num_sms=148, num_warps=4) -> Mapping:
     """deriveProgramMappingPlan, lib/Analysis/ProgramMappingPlan.cpp:329-458,
     deriveReductionPlan (ReductionPlan.cpp:137-192) and the mainline kind of
     ResourceClosurePlan.cpp:154-161."""
@@ -106,6 +109,8 @@ def program_mapping(m, n, k, bm, bn, bk, group_m=8, split_k=1, persistent=False,
         kind, span_m, span_n = "tile", 1, tn
         ppg, groups, total = tn, tm, tm * tn
         mainline = "single_tile"
+    if num_sms > 0 and num_warps > MAX_WARPS_PER_CTA:  # ProgramMappingPlan.cpp:446-449
+        raise ValueError("num_warps exceeds target max warps per CTA")
     if persistent and num_ctas > num_sms:
         num_ctas = num_sms
     return Mapping(kind, tm, tn, tk, span_m, span_n, ppg, groups, total, s, num_ctas, red, mainline)

@@ -31,6 +31,22 @@ int main(void) {
   d.block_m = 40;
   if (tb_matmul_plan_create(&d, -1, &plan) != TB_ERR_INVALID_ARGUMENT) return 5;
   printf("rejected: %s\n", tb_last_error());
+  /* N-shard: columns of each of 3 ranks for 8192 columns of 256-wide tiles */
+  tb_matmul_desc big;
+  tb_matmul_desc_init(&big);
+  big.m = 8192; big.n = 8192; big.k = 8192;
+  big.block_m = 256; big.block_n = 256; big.block_k = 64;
+  big.num_warps = 4; big.num_stages = 4;
+  if (tb_matmul_plan_create(&big, -1, &plan) != TB_OK) return 6;
+  for (int r = 0; r < 3; ++r) {
+    int64_t c0 = 0, nc = 0;
+    size_t ws = 1;
+    if (tb_matmul_nshard_columns(plan, r, 3, &c0, &nc) != TB_OK) return 7;
+    if (tb_matmul_nshard_workspace_bytes(plan, r, 3, &ws) != TB_OK) return 8;
+    printf("nshard rank %d: columns %lld + %lld, workspace %zu\n", r, (long long)c0, (long long)nc, ws);
+  }
+  if (tb_matmul_nshard_columns(plan, 3, 3, NULL, NULL) != TB_ERR_INVALID_ARGUMENT) return 9;
+  tb_matmul_plan_destroy(plan);
   printf("version: %s\n", tb_version());
   return 0;
 }

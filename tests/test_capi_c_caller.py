@@ -30,3 +30,7 @@ def test_plain_c_caller(tmp_path):
     assert "pid 0 -> tile (0, 0)" in text and "pid 1 -> tile (1, 0)" in text and "pid 2 -> tile (0, 1)" in text
     assert "pid 4 -> tile (2, 0)" in text and "pid 5 -> tile (2, 1)" in text
     assert "rejected: stage1 requires block_m % 16 == 0" in text
+    # N-shard columns: 32 tiles of 256 over 3 ranks -> 11, 11, 10 tiles
+    assert "nshard rank 0: columns 0 + 2816, workspace 0" in text
+    assert "nshard rank 1: columns 2816 + 2816" in text
+    assert "nshard rank 2: columns 5632 + 2560" in text

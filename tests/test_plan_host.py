@@ -71,13 +71,56 @@ def test_split_k_below_one_is_clamped_like_the_reference():
     assert p.info["mapping_kind"] == "tile" and p.info["split_k"] == 1
 
 
-def test_unsupported_tiles_are_reported():
-    with pytest.raises(tb.TBError) as e:
-        plan(1024, 1024, 64, 512, 64, 32)
-    assert e.value.code == 2
-    with pytest.raises(tb.TBError) as e:
-        plan(1024, 1024, 64, 128, 640, 32, exact_tile=False)
-    assert e.value.code == 2
+def test_num_warps_limit_matches_reference():
+    """ProgramMappingPlan.cpp:446-449: more than maxWarpsPerCTA = 8 warps
+    (TargetInfo.cpp:126) is rejected once the target's SM count is known."""
+    p = plan(256, 256, 64, 128, 128, 32, num_warps=8)
+    assert p.info["num_warps"] == 8
+    for nw in (9, 16, 32):
+        with pytest.raises(tb.TBError) as e:
+            plan(256, 256, 64, 128, 128, 32, num_warps=nw)
+        assert e.value.code == 1 and e.value.message == "num_warps exceeds target max warps per CTA"
+        with pytest.raises(ValueError, match="num_warps exceeds target max warps per CTA"):
+            om.program_mapping(256, 256, 64, 128, 128, 32, num_warps=nw)
+
+
+@pytest.mark.parametrize("bm,bn,tile,sub", [
+    (512, 256, "tb_gemm_sm100_pair_256x256", [2, 1]),
+    (256, 1024, "tb_gemm_sm100_pair_256x256", [1, 4]),
+    (512, 128, "tb_gemm_sm100_pair_256x128", [2, 1]),
+    (128, 640, "tb_gemm_sm100_128x256", [1, 3]),
+    (384, 384, "tb_gemm_sm100_pair_256x512", [2, 1]),
+    (272, 64, "tb_gemm_sm100_pair_256x128", [2, 1]),
+])
+def test_large_program_tiles_run_as_subtiles(bm, bn, tile, sub):
+    """KernelConfig.cpp:217-221 only asks block_m % 16 and block_n % 8: a
+    program tile larger than every hardware tile runs as sub-tiles, with the
+    reference's program mapping unchanged."""
+    m, n = 2 * bm + 16, 3 * bn
+    p = plan(m, n, 256, bm, bn, 64, exact_tile=False)
+    info = p.info
+    assert info["kernel"] == tile and info["program_subtiles"] == sub
+    want = om.program_mapping(m, n, 256, bm, bn, 64)
+    assert info["total_programs"] == want.total_programs
+    assert info["work_items"] == want.total_programs * sub[0] * sub[1]
+    assert info["fused_program_pairs"] == "none"
+
+
+def test_tail_split_plan_facts():
+    """8192 x 1024 x 8192 (one rank of an 8-way N-shard): 128 pair items on
+    74 CTA pairs leave the second wave 73 % full; the plan cuts every item
+    into K pieces. f16 C, beta = 0 and deterministic plans keep whole items."""
+    p = plan(8192, 1024, 8192, 256, 256, 64)
+    ts = p.info["tail_split"]
+    assert ts is not None and ts["whole_items"] + ts["split_items"] == p.info["work_items"] == 128
+    assert ts["k_pieces"] >= 2
+    assert p.info["walk_positions"] == ts["whole_items"] + ts["split_items"] * ts["k_pieces"]
+    assert p.info["grid"] == 148
+    for kw in (dict(c_dtype="f16"), dict(beta=0), dict(deterministic=True), dict(split_k=2)):
+        q = plan(8192, 1024, 8192, 256, 256, 64, **kw)
+        assert q.info["tail_split"] is None, kw
+    # 8192^3 (1024 items, 13.8 waves) gains too little to split
+    assert plan(8192, 8192, 8192, 256, 256, 64).info["tail_split"] is None
 
 
 # ---------------------------------------------------------------- mapping
@@ -289,3 +332,19 @@ def test_random_mappings_match_oracle(m, n, k, bm, bn, bk, group_m, split_k, per
     assert info["total_programs"] == want.total_programs
     for pid in range(0, want.total_programs, max(1, want.total_programs // 512)):
         assert p.program_work(pid) == om.program_work(want, pid), pid
+
+
+@pytest.mark.parametrize("n,bn,world", [(8192, 256, 8), (8192, 256, 3), (1000, 64, 4), (100, 64, 4),
+                                        (4096, 128, 5)])
+def test_nshard_columns_match_partition(n, bn, world):
+    """tb_matmul_nshard_columns gives each rank whole block_n tiles, balanced,
+    covering [0, n) once — the partition parallel.column_shard states."""
+    from mini_triton_nvgpu_v1_b200 import parallel as par
+    cfg = tb.KernelConfig(m=512, n=n, k=128, block_m=128, block_n=bn, block_k=64, exact_tile=False)
+    end = 0
+    for r in range(world):
+        sh = par.NShard(cfg, r, world)
+        assert (sh.col0, sh.ncols) == par.column_shard(n, world, r, bn)
+        assert sh.col0 == end
+        end += sh.ncols
+    assert end == n

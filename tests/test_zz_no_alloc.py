@@ -9,7 +9,7 @@ instead of a caller-provided workspace.
 
 These tests call that entry point through the C ABI (ctypes, raw device
 pointers) and check it against the regular entry point, tb_matmul_run with a
-caller-owned workspace, on two calls in a row. The file is named so pytest
+caller-owned workspace, and against the CPU oracle, on two calls in a row. The file is named so pytest
 collects it last; it must pass both alone in a fresh process (the first call
 on the device sets the scratch address up) and after the other tests.
 """
@@ -20,6 +20,7 @@ import ctypes as C
 import numpy as np
 import pytest
 
+import oracle
 from conftest import make_inputs
 
 pytestmark = pytest.mark.gpu
@@ -78,6 +79,11 @@ def test_no_alloc_matches_regular_entry_point_twice(cuda, shape, knobs):
         torch.cuda.synchronize()
         err = float((got - want).abs().max())
         assert err <= tol, f"call {call}: max|Δ| vs tb_matmul_run = {err} > {tol}"
+        # and against the CPU oracle, so a fault the two entry points share
+        # cannot pass unseen
+        ref = oracle.matmul_ref(A, B, Cin)
+        err_ref = float(np.abs(got.cpu().numpy() - ref).max())
+        assert err_ref <= tol, f"call {call}: max|Δ| vs the oracle = {err_ref} > {tol}"
 
 
 def test_no_alloc_rejects_plans_beyond_the_scratch(cuda):
