@@ -791,6 +791,192 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- small
+// Latency kernel for problems whose every work item has at most kSmallK K
+// elements on a one-CTA 128 × BN tile (the BASELINE's 64×64×32, 96×80×32,
+// 192×128×32 and split 64×64×64 programs). No tensor maps, no warp roles, no
+// pipeline: all 128 threads copy the item's A rows, B rows and C_in row into
+// shared memory at once with cp.async — A and B straight into the
+// 128-byte-swizzled layout the UMMA descriptors read (16-byte chunk j of row r
+// at chunk j ^ (r % 8)), zero-filled past the item's K range and past M/N —
+// then one thread issues the K/16 tcgen05.mma steps, and every thread takes
+// its accumulator row from TMEM and stores it. A CTA walks several items in
+// turn when there are more items than CTAs (persistent plans).
+constexpr int kSmallK = 128;
+constexpr uint32_t kSmallASub = 128 * 64 * 2;         // one [128 m × 64 k] K-major sub-tile
+constexpr uint32_t kSmallABytes = kSmallK / 64 * kSmallASub;
+constexpr uint32_t kSmallBox = kSmallK * 64 * 2;      // one [kSmallK k × 64 n] MN-major box
+
+template <int BN, typename OutT>
+struct SmallCfg {
+  static constexpr uint32_t kBBytes = BN / 64 * kSmallBox;
+  static constexpr uint32_t kCinStride = BN * sizeof(OutT) + 16;  // padded row: conflict-free reads
+  static constexpr size_t kSmem = 1024 + kSmallABytes + kBBytes + 128 * kCinStride + 64;
+};
+
+template <int BN, typename OutT>
+__global__ void __launch_bounds__(128, 1)
+    tb_gemm_small_kernel(const KParams p, const uint16_t* __restrict__ A, int64_t lda,
+                         const uint16_t* __restrict__ B, int64_t ldb) {
+  using Sc = SmallCfg<BN, OutT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kSmallABytes;
+  uint8_t* sCin = sB + Sc::kBBytes;
+  uint64_t* done = reinterpret_cast<uint64_t*>(sCin + 128 * Sc::kCinStride);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 1);
+  const int t = threadIdx.x;
+  const int warp = t / 32;
+  if (t == 0) {
+    mbar_init(smem_addr(done), 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_addr(tmem_holder), BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const uint32_t idesc = idesc_f16_f32(128, BN, 0, 1);
+  uint32_t phase = 0;
+  for (int32_t pos = blockIdx.x; pos < p.positions; pos += gridDim.x) {
+    const Extent e = program_extent<128, BN>(p, pos, kSmallK);
+    const int kvalid = e.nkb > 0 ? e.k_end - e.k_begin : 0;  // <= kSmallK (plan rule)
+    const int k16 = (kvalid + 15) / 16 * 16;                 // K covered by the MMA steps
+    // ---- stage A (K-major, two [128 × 64] sub-tiles) and B (MN-major
+    //      [kSmallK × 64] boxes), 16-byte chunks, zero past K / M / N
+    for (int c = t; c < 128 * (k16 / 8); c += 128) {
+      const int r = c / (k16 / 8), kc = c % (k16 / 8);   // row, 8-element K chunk
+      const int k = kc * 8;
+      const int64_t gm = (int64_t)e.m0 + r;
+      uint32_t bytes = 0;
+      const uint16_t* src = A;
+      if (gm < p.M && k < kvalid) {
+        bytes = (uint32_t)min(16, (kvalid - k) * 2);
+        src = A + gm * lda + e.k_begin + k;
+      }
+      const uint32_t dst = smem_addr(sA + (k / 64) * kSmallASub + r * 128 + (((k / 8) % 8) ^ (r % 8)) * 16);
+      cp_async_16(dst, src, bytes);
+    }
+    for (int c = t; c < k16 * (BN / 8); c += 128) {
+      const int kr = c / (BN / 8), nc = c % (BN / 8);    // K row, 8-column chunk
+      const int64_t gn = (int64_t)e.n0 + nc * 8;
+      uint32_t bytes = 0;
+      const uint16_t* src = B;
+      if (kr < kvalid && gn < p.N) {
+        bytes = (uint32_t)(p.N - gn >= 8 ? 16 : (p.N - gn) * 2);
+        src = B + (int64_t)(e.k_begin + kr) * ldb + gn;
+      }
+      const uint32_t dst = smem_addr(sB + (nc / 8) * kSmallBox + kr * 128 + ((nc % 8) ^ (kr % 8)) * 16);
+      cp_async_16(dst, src, bytes);
+    }
+    // ---- this thread's C_in row, fetched alongside the operands
+    const bool row_ok = t < e.rows;
+    const int64_t grow = (int64_t)e.m0 + t;
+    const bool cin_smem = p.cin_smem && p.beta && p.epilogue == kEpiStore && row_ok;
+    uint8_t* cin_row = sCin + (size_t)t * Sc::kCinStride;
+    if (cin_smem) {
+      const char* src = reinterpret_cast<const char*>(reinterpret_cast<const OutT*>(p.C) + grow * p.ldc + e.n0);
+      const int bytes = e.cols * (int)sizeof(OutT);
+      for (int off = 0; off < bytes; off += 16)
+        cp_async_16(smem_addr(cin_row + off), src + off, (uint32_t)min(16, bytes - off));
+    }
+    cp_async_wait_all();
+    fence_proxy_async_smem();  // cp.async wrote through the generic proxy; the MMA reads via async
+    __syncthreads();
+    if (t == 0 && k16 > 0) {
+      tc_fence_after();
+      const uint64_t da0 = smem_desc_sw128(smem_addr(sA), 16, 1024);
+      const uint64_t db0 = smem_desc_sw128(smem_addr(sB), kSmallBox, 1024);
+      for (int kk = 0; kk < k16 / 16; ++kk) {
+        const uint64_t da = da0 + (uint64_t)((((kk >> 2) * kSmallASub) + (kk & 3) * 32) >> 4);
+        const uint64_t db = db0 + (uint64_t)((kk * 2048) >> 4);
+        umma_f16(tmem_base, da, db, idesc, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(smem_addr(done));
+    }
+    if (k16 > 0) {
+      // every thread waits (bounded) for the MMAs
+      const long long t0 = clock64();
+      while (!mbar_try_wait(smem_addr(done), phase)) {
+        if (clock64() - t0 > kWaitBudgetCycles) {
+          record_error(TB_ERR_DEVICE_TIMEOUT, kSiteEpilogue);
+          break;
+        }
+      }
+      phase ^= 1u;
+      tc_fence_after();
+    }
+    // ---- epilogue: thread t owns row t of the tile (TMEM lane t)
+    for (int c0 = 0; c0 < e.cols; c0 += 32) {
+      float v[32];
+      if (k16 > 0) {
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      if (!row_ok) continue;
+      const int ncol = min(32, e.cols - c0);
+      const int64_t gcol = (int64_t)e.n0 + c0;
+      if (p.epilogue == kEpiStore) {
+        OutT* dst = reinterpret_cast<OutT*>(p.C) + grow * p.ldc + gcol;
+        if (p.beta) {
+          if (cin_smem) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              float c = 0.f;
+              if constexpr (sizeof(OutT) == 4) c = reinterpret_cast<const float*>(cin_row)[c0 + i];
+              else c = __half2float(reinterpret_cast<const __half*>(cin_row)[c0 + i]);
+              if (i < ncol) v[i] += c;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < ncol) v[i] += OutIO<OutT>::load(dst + i);
+          }
+        }
+        if (p.ex.any) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < ncol) v[i] = apply_exprs(p.ex, v[i], gcol + i);
+        }
+        if (ncol == 32 && p.vec_c) {
+          OutIO<OutT>::store32(dst, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < ncol) OutIO<OutT>::store(dst + i, v[i]);
+        }
+      } else if (p.epilogue == kEpiWorkspace) {
+        float* dst = p.ws + ((int64_t)e.part * p.M + grow) * p.N + gcol;
+        if (ncol == 32 && p.vec_ws) {
+          OutIO<float>::store32(dst, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < ncol) dst[i] = v[i];
+        }
+      } else {  // kEpiAtomic: f32 C only
+        float* dst = reinterpret_cast<float*>(p.C) + grow * p.ldc + gcol;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < ncol) atomicAdd(dst + i, v[i]);
+      }
+    }
+    // the next item overwrites shared memory and TMEM
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+  if (warp == 0) tmem_dealloc(tmem_base, BN);
+}
+
 // C = beta·C_in + Σ_s ws[s] in a fixed order (split_k_serial): deterministic.
 // HBM bound; every thread keeps up to 8 partial loads in flight. Launched
 // with programmatic dependent launch: the grid may start while the GEMM
@@ -1002,6 +1188,37 @@ tbStatus dispatch_tile(const tb_matmul_plan* plan, const CUtensorMap& ta, const 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+std::atomic<bool> g_small_attr_set[2][2][kMaxDevices];
+
+template <int BN, typename OutT>
+tbStatus launch_small_bn(const tb_matmul_plan* plan, const KParams& kp, const void* A, int64_t lda,
+                         const void* B, int64_t ldb, cudaStream_t stream, int ot) {
+  auto kern = tb_gemm_small_kernel<BN, OutT>;
+  constexpr size_t smem = SmallCfg<BN, OutT>::kSmem;
+  const int bi = BN == 64 ? 0 : 1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices || !g_small_attr_set[bi][ot][dev].load()) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess)
+      return tb_fail(TB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    if (dev >= 0 && dev < kMaxDevices) g_small_attr_set[bi][ot][dev].store(true);
+  }
+  kern<<<(unsigned)plan->grid, 128, smem, stream>>>(kp, static_cast<const uint16_t*>(A), lda,
+                                                    static_cast<const uint16_t*>(B), ldb);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return tb_fail(TB_ERR_CUDA, std::string("tb_gemm_small launch: ") + cudaGetErrorString(e));
+  return TB_OK;
+}
+
+template <typename OutT>
+tbStatus launch_small(const tb_matmul_plan* plan, const KParams& kp, const void* A, int64_t lda,
+                      const void* B, int64_t ldb, cudaStream_t stream, int ot) {
+  return plan->cta_n == 64 ? launch_small_bn<64, OutT>(plan, kp, A, lda, B, ldb, stream, ot)
+                           : launch_small_bn<128, OutT>(plan, kp, A, lda, B, ldb, stream, ot);
+}
+
 tbStatus pack_rows_f16(const void* src, int64_t ld_src, void* dst, int64_t ld_dst, int64_t rows,
                        int64_t cols, int num_sms, cudaStream_t stream) {
   const int64_t total = rows * ld_dst;
@@ -1028,6 +1245,11 @@ size_t tb_kernel_smem_bytes(int32_t kernel_tile, int32_t /*stages*/) {
     case kTile256x512: return Cfg<512, 2>::kSmem;
   }
   return 0;
+}
+
+size_t tb_small_smem_bytes(int32_t cta_n, int32_t c_dtype) {
+  if (cta_n == 64) return c_dtype == TB_F16 ? SmallCfg<64, __half>::kSmem : SmallCfg<64, float>::kSmem;
+  return c_dtype == TB_F16 ? SmallCfg<128, __half>::kSmem : SmallCfg<128, float>::kSmem;
 }
 
 int32_t tb_kernel_kb(int32_t kernel_tile) {
@@ -1119,12 +1341,17 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   }
 
   CUtensorMap ta, tbm;
-  if (d.a_col_major)  // storage k × m (m contiguous): [64 k × 64 m] boxes
+  memset(&ta, 0, sizeof(ta));
+  memset(&tbm, 0, sizeof(tbm));
+  if (plan->small) {
+    // the latency kernel stages operands with cp.async: no tensor maps
+  } else if (d.a_col_major)  // storage k × m (m contiguous): [64 k × 64 m] boxes
     st = encode_f16_2d(&ta, A, d.k, d.m, lda, (uint32_t)plan->kb, "A");
   else                // storage m × k: [128 m × 64 k] boxes
     st = encode_f16_2d(&ta, A, d.m, d.k, lda, kCtaM, "A");
   if (st != TB_OK) return st;
-  if (d.b_col_major)  // storage n × k (k contiguous): [BN/G n × 64 k] boxes; the 256 × 512
+  if (plan->small) {
+  } else if (d.b_col_major)  // storage n × k (k contiguous): [BN/G n × 64 k] boxes; the 256 × 512
                       // pair tile loads its 256 columns per CTA as two 128-row boxes
     st = encode_f16_2d(&tbm, B, d.n, d.k, ldb,
                        (uint32_t)(plan->cta_n > 256 ? 128 : plan->cta_n / plan->ctas_per_tile), "B");
@@ -1180,7 +1407,8 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   CUtensorMap tcm;
   memset(&tcm, 0, sizeof(tcm));
   kp.tma_out = kTmaNone;
-  const bool exact_hw_tile =
+  if (plan->small) kp.cin_smem = kp.vec_c;  // every item stages its C_in rows (direct epilogue)
+  const bool exact_hw_tile = !plan->small &&
       d.block_m * (plan->fuse == 1 || plan->fuse == 4 ? 2 : 1) == (int64_t)plan->cta_m * plan->sub_m &&
       d.block_n * (plan->fuse >= 2 ? 2 : 1) == (int64_t)plan->cta_n * plan->sub_n;
   if (exact_hw_tile && d.c_dtype == TB_F32 && aligned16(Cp) && ldc % 4 == 0) {
@@ -1216,8 +1444,12 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
                                       std::to_string((int)r));
   }
 
-  st = d.c_dtype == TB_F16 ? dispatch_tile<__half>(plan, ta, tbm, tcm, kp, stream, 1)
-                           : dispatch_tile<float>(plan, ta, tbm, tcm, kp, stream, 0);
+  if (plan->small)
+    st = d.c_dtype == TB_F16 ? launch_small<__half>(plan, kp, A, lda, B, ldb, stream, 1)
+                             : launch_small<float>(plan, kp, A, lda, B, ldb, stream, 0);
+  else
+    st = d.c_dtype == TB_F16 ? dispatch_tile<__half>(plan, ta, tbm, tcm, kp, stream, 1)
+                             : dispatch_tile<float>(plan, ta, tbm, tcm, kp, stream, 0);
   if (st != TB_OK) return st;
 
   if (plan->epilogue == kEpiWorkspace) {

@@ -468,6 +468,18 @@ tbStatus tb_plan_build(const tb_matmul_desc& d, int device, int num_sms, tb_matm
                          &p.tail_parts);
   p.positions = p.dp_items + p.tail_items * p.tail_parts;
   p.grid = p.ctas_per_tile * std::max<int64_t>(1, std::min<int64_t>(p.positions, resident));
+  // Small problems (every item's K range within 128 elements on a one-CTA
+  // tile at most 128 wide) are launch- and latency-bound: they run on the
+  // latency kernel, which skips the tensor maps and the warp-role pipeline.
+  const int64_t k_item = std::min<int64_t>(d.k, ceil_div(tiles_k, split_k) * d.block_k);
+  p.small = !big && p.ctas_per_tile == 1 && p.cta_n <= 128 && k_item <= 128 && !d.a_col_major &&
+            !d.b_col_major && p.tail_items == 0 && p.positions <= 4 * (p.grid / p.ctas_per_tile);
+  if (p.small) {
+    p.stages = 1;
+    p.kb = 128;
+    p.smem_bytes = tb_small_smem_bytes(p.cta_n, d.c_dtype);
+    p.tmem_cols = p.cta_n;
+  }
 
   return TB_OK;
 }
@@ -510,6 +522,7 @@ extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* bu
     return TB_OK;
   }
   const tb_matmul_desc& d = plan->desc;
+  const char* small_names[] = {"tb_gemm_sm100_small_128x64", "tb_gemm_sm100_small_128x128"};
   const char* kernel_names[] = {"tb_gemm_sm100_128x64", "tb_gemm_sm100_128x128",
                                 "tb_gemm_sm100_128x256", "tb_gemm_sm100_pair_256x128",
                                 "tb_gemm_sm100_pair_256x256", "tb_gemm_sm100_pair_256x512"};
@@ -544,7 +557,9 @@ extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* bu
   o << "\"resident_programs\": " << plan->resident_programs << ", ";
   o << "\"selected_mainline_kind\": \"" << plan->mainline_kind << "\", ";
   o << "\"num_sms\": " << plan->num_sms << ", ";
-  o << "\"kernel\": \"" << kernel_names[plan->kernel_tile] << "\", ";
+  o << "\"kernel\": \""
+    << (plan->small ? small_names[plan->kernel_tile == kTile128x64 ? 0 : 1] : kernel_names[plan->kernel_tile])
+    << "\", ";
   o << "\"cta_tile\": [" << plan->cta_m << ", " << plan->cta_n << ", " << plan->kb << "], ";
   o << "\"ctas_per_tile\": " << plan->ctas_per_tile << ", ";
   o << "\"fused_program_pairs\": \""

@@ -69,6 +69,10 @@ struct tb_matmul_plan {
   // whole work items, the last tail_items items run as tail_parts K pieces
   // each (reduce-added into C); positions = dp_items + tail_items·tail_parts.
   int64_t dp_items, tail_items, tail_parts, positions;
+  // Latency kernel (tb_gemm_small_kernel): one-CTA tiles at most 128 wide,
+  // every work item at most 128 K elements, row-major operands, at most
+  // four items per CTA.
+  bool small;
   int32_t cta_m, cta_n;        // hardware tile (cta_m = 256: a CTA pair)
   int32_t ctas_per_tile;       // 1 or 2
   int32_t stages;              // shared-memory ring depth
@@ -93,6 +97,7 @@ tbStatus tb_launch(const tb_matmul_plan* plan, const void* A, int64_t lda,
 size_t tb_kernel_smem_bytes(int32_t kernel_tile, int32_t stages);
 int32_t tb_kernel_max_stages(int32_t kernel_tile);
 int32_t tb_kernel_kb(int32_t kernel_tile);
+size_t tb_small_smem_bytes(int32_t cta_n, int32_t c_dtype);
 
 // Derives a concrete plan for `d` (validated) into *out; tb_plan.cpp.
 tbStatus tb_plan_build(const tb_matmul_desc& d, int device, int num_sms, tb_matmul_plan* out);

@@ -245,8 +245,8 @@ def test_workspace_bytes():
 
 
 def test_hardware_tile_selection():
-    assert plan(64, 64, 32, 64, 64, 32).info["kernel"] == "tb_gemm_sm100_128x64"
-    assert plan(96, 80, 32, 128, 128, 64, exact_tile=False).info["kernel"] == "tb_gemm_sm100_128x128"
+    assert plan(64, 64, 256, 64, 64, 32).info["kernel"] == "tb_gemm_sm100_128x64"
+    assert plan(96, 80, 320, 128, 128, 64, exact_tile=False).info["kernel"] == "tb_gemm_sm100_128x128"
     assert plan(8192, 8192, 8192, 128, 256, 64, group_m=3).info["kernel"] == "tb_gemm_sm100_128x256"
     info = plan(8192, 8192, 8192, 256, 256, 64).info
     assert info["kernel"] == "tb_gemm_sm100_pair_256x256" and info["ctas_per_tile"] == 2
@@ -348,3 +348,21 @@ def test_nshard_columns_match_partition(n, bn, world):
         assert sh.col0 == end
         end += sh.ncols
     assert end == n
+
+
+@pytest.mark.parametrize("shape,knobs,kernel", [
+    ((64, 64, 32), dict(block_m=64, block_n=64, block_k=32), "tb_gemm_sm100_small_128x64"),
+    ((96, 80, 32), dict(block_m=128, block_n=128, block_k=64, exact_tile=False), "tb_gemm_sm100_small_128x128"),
+    ((192, 128, 32), dict(block_m=64, block_n=64, block_k=32, group_m=8), "tb_gemm_sm100_small_128x64"),
+    ((64, 64, 64), dict(block_m=64, block_n=64, block_k=32, split_k=2), "tb_gemm_sm100_small_128x64"),
+    ((192, 128, 32), dict(block_m=64, block_n=64, block_k=32, persistent=True, num_ctas=2),
+     "tb_gemm_sm100_small_128x128"),
+    ((512, 512, 512), dict(block_m=128, block_n=128, block_k=64), "tb_gemm_sm100_pair_256x128"),
+    ((64, 64, 256), dict(block_m=64, block_n=64, block_k=32), "tb_gemm_sm100_128x64"),
+    ((64, 512, 32), dict(block_m=64, block_n=512, block_k=32), "tb_gemm_sm100_pair_256x512"),
+])
+def test_small_problems_take_the_latency_kernel(shape, knobs, kernel):
+    """Every work item within 128 K elements on a one-CTA tile at most 128
+    wide: the latency kernel; anything else: the pipelined kernels."""
+    m, n, k = shape
+    assert tb.MatmulPlan(tb.KernelConfig(m=m, n=n, k=k, **knobs)).info["kernel"] == kernel
