@@ -57,6 +57,7 @@ def parse():
     ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "splitk", "sweep"],
                     help="gemm8192: the headline 8192^3 N-sharded GEMM; splitk: the skinny "
                          "512x512x65536 split-K config (K-sharded + reduce-scatter at N>1)")
+    ap.add_argument("--only", default=None, help="sweep: only the configs whose name contains this")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
                     help="gemm8192 at N>1: strong = the fixed 8192^3 problem split along N "
                          "(BASELINE's config); weak = 8192 columns per GPU")
@@ -583,6 +584,18 @@ SWEEP = [
      dict(block_m=256, block_n=256, block_k=64, persistent=True, num_ctas=148), "f16", "tensor"),
     ("persistent 16384^3 (pair, grid=SMs, f16 out)", 16384, 16384, 16384,
      dict(block_m=256, block_n=256, block_k=64, persistent=True, num_ctas=148), "f16", "tensor"),
+    # one rank's slice of the 8192^3 problem N-sharded over 2 / 4 / 8 GPUs,
+    # with the tail split (default) and with whole items (deterministic)
+    ("N-shard slice 1/2: 8192x4096x8192", 8192, 4096, 8192,
+     dict(block_m=256, block_n=256, block_k=64, group_m=8), "f32", "tensor"),
+    ("N-shard slice 1/4: 8192x2048x8192", 8192, 2048, 8192,
+     dict(block_m=256, block_n=256, block_k=64, group_m=8), "f32", "tensor"),
+    ("N-shard slice 1/4, whole items", 8192, 2048, 8192,
+     dict(block_m=256, block_n=256, block_k=64, group_m=8, deterministic=True), "f32", "tensor"),
+    ("N-shard slice 1/8: 8192x1024x8192", 8192, 1024, 8192,
+     dict(block_m=256, block_n=256, block_k=64, group_m=8), "f32", "tensor"),
+    ("N-shard slice 1/8, whole items", 8192, 1024, 8192,
+     dict(block_m=256, block_n=256, block_k=64, group_m=8, deterministic=True), "f32", "tensor"),
 ]
 
 
@@ -598,7 +611,10 @@ def run_sweep(args):
     peak_b, peak_s, _ = peaks()
     hbm = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("hbm_gbs", 6650.0) \
         if (ROOT / "MEASURED_PEAKS.json").exists() else 6650.0
+    only = getattr(args, "only", None)
     for name, m, n, k, kn, cdt, bound in SWEEP:
+        if only and only not in name:
+            continue
         g = torch.Generator(device=dev).manual_seed(2)
         A = (torch.rand(m, k, device=dev, generator=g) * 2 - 1).half()
         B = (torch.rand(k, n, device=dev, generator=g) * 2 - 1).half()

@@ -34,6 +34,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <type_traits>
 #include <cstring>
 #include <cstdio>
 #include <mutex>
@@ -141,6 +142,7 @@ struct KParams {
   int32_t tma_out;   // TmaOut: f32 tile output written by TMA from swizzled shared staging
   int32_t fuse;      // program pairing (plan.fuse): work item w runs programs 2w and 2w+1
   int32_t cin_smem;  // one work item per CTA: the epilogue stages C_in through the idle ring
+  int32_t one_item;  // every CTA (pair) runs at most one work item: the ring is idle in its epilogue
   int32_t walk_grouped;  // tb::WalkMode: the order resident CTAs take work items in
   int32_t work_items;    // hardware work items (programs × sub-tiles, or fused programs)
   int32_t positions;     // walk positions: dp_items + tail_items · tail_parts
@@ -332,7 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = bars + 2 * S;   // every CTA: accumulator ready
   uint64_t* tempty = bars + 2 * S + 2;  // leader: accumulator drained by all epilogues
   uint64_t* drain = bars + 2 * S + 4;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  uint64_t* cinbar = bars + 2 * S + 5;  // per epilogue warp: C_in chunks loaded by TMA
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
@@ -352,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_addr(&tempty[a]), 4 * G);
     }
     mbar_init(smem_addr(drain), 1);
+    for (int w = 0; w < 4; ++w) mbar_init(smem_addr(&cinbar[w]), 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -598,6 +602,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = (int)rank * 128 + q * 32 + lane;
     uint8_t* epi_buf = sEpi + (size_t)(warp - 2) * 2 * Cf::kEpiBufBytes;
     uint32_t epi_slot = 0;
+    // 128-byte staging rows: 32 f32 or 64 f16 columns per chunk
+    constexpr int kChunkCols = 128 / (int)sizeof(OutT);
+    constexpr uint32_t kRingWarp = (uint32_t)S * Cf::kStageBytes / 4;  // ring bytes per epilogue warp
+    constexpr int kRingSlots = (int)(kRingWarp / Cf::kEpiBufBytes);
+    uint32_t cin_phase = 0;
+    if (p.one_item && p.beta && p.epilogue == kEpiStore && first_pid < p.positions) {
+      // One item per CTA: its C_in rows are prefetched into L2 while the
+      // mainloop runs, so the epilogue's C_in loads hit L2.
+      const Extent e0 = program_extent<kCtaM * G, BN>(p, first_pid, Cf::kKB);
+      const uint32_t bytes = (uint32_t)(e0.cols * (int)sizeof(OutT)) & ~15u;
+      if (row_in_tile < e0.rows && bytes > 0 && p.vec_c) {
+        const char* src = reinterpret_cast<const char*>(reinterpret_cast<const OutT*>(p.C) +
+                                                        ((int64_t)e0.m0 + row_in_tile) * p.ldc + e0.n0);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+      }
+    }
     const uint32_t tempty_leader0 = G == 2 ? map_to_cta(smem_addr(&tempty[0]), 0) : smem_addr(&tempty[0]);
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -623,7 +643,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // per-row reads then spread over all banks.
       constexpr uint32_t kCinStride = (uint32_t)(BN * sizeof(OutT)) + 16u;
       constexpr bool kCinFits = 128u * kCinStride <= (uint32_t)S * Cf::kStageBytes;
-      const bool cin_from_smem = kCinFits && p.cin_smem && p.beta && p.epilogue == kEpiStore && row_ok;
+      const bool cin_from_smem = kCinFits && p.cin_smem && p.beta && p.epilogue == kEpiStore && row_ok &&
+                                 !(tma_out != kTmaNone && p.one_item &&
+                                   (e.cols + kChunkCols - 1) / kChunkCols <= kRingSlots);
       const uint8_t* cin_row = smem + (size_t)((warp - 2) * 32 + lane) * kCinStride;
       if (cin_from_smem) {
         fence_proxy_async_smem();
@@ -665,6 +687,146 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) c[i] = i < ncol ? OutIO<OutT>::load(src + i) : 0.f;
         }
       };
+      if (tma_out != kTmaNone) {
+        // TMA path (program tile == hardware tile, or a whole sub-tile of
+        // one). The warp's 32 rows go out in chunks of 32 × 128 bytes (32 f32
+        // or 64 f16 columns) staged in 128-byte-swizzled shared memory (row
+        // r's 16-byte piece j at piece j ^ (r % 8): the warp's 16-byte writes
+        // are bank-conflict free), written, reduce-added or stored by TMA;
+        // rows/columns past M/N are clipped by TMA, so rows past M carry zeros.
+        // Two staging buffers per warp rotate; with one work item per CTA
+        // (wide) the idle ring holds all of the warp's chunks at once, C_in
+        // comes in by TMA into the same buffers, and no chunk waits for the
+        // previous one's store.
+        // chunk element: OutT for C stores; f32 for reduce-adds and the
+        // split_k_serial workspace
+        bool wide = false;
+        auto chunks = [&](auto f16_tag) -> bool {
+          constexpr bool kF16 = decltype(f16_tag)::value;
+          constexpr int kCw = kF16 ? 64 : 32;
+          const int nch = (e.cols + kCw - 1) / kCw;
+          wide = p.one_item && nch <= kRingSlots;
+          uint8_t* slots = wide ? smem + (size_t)(warp - 2) * kRingWarp : epi_buf;
+          const bool cin_tma = wide && tma_out == kTmaStoreC && p.beta;
+          const int32_t y0 = (int32_t)(grow - lane);
+          if (cin_tma) {
+            const uint32_t cb = smem_addr(&cinbar[q]);
+            if (lane == 0) {
+              fence_proxy_async_smem();
+              mbar_expect_tx(cb, (uint32_t)nch * Cf::kEpiBufBytes);
+              for (int j = 0; j < nch; ++j)
+                tma_load_2d(smem_addr(slots + (size_t)j * Cf::kEpiBufBytes), &tmC, cb,
+                            (int32_t)(e.n0 + j * kCw), y0);
+            }
+            int okc = 0;
+            if (lane == 0) okc = wait_bounded(cb, cin_phase, abort_flag, kSiteEpilogue);
+            okc = __shfl_sync(0xffffffffu, okc, 0);
+            cin_phase ^= 1u;
+            if (!okc) return false;
+          }
+          for (int j = 0; j < nch; ++j) {
+            const int c0 = j * kCw;
+            const int64_t gcol = (int64_t)e.n0 + c0;
+            uint8_t* buf = wide ? slots + (size_t)j * Cf::kEpiBufBytes
+                                : epi_buf + (size_t)(epi_slot & 1) * Cf::kEpiBufBytes;
+            if (!wide) {
+              // The bulk op issued two chunks ago must have finished reading buf.
+              if (lane == 0) bulk_wait_group_read<1>();
+              __syncwarp();
+            }
+            uint8_t* row = buf + lane * 128;
+  #pragma unroll
+            for (int h = 0; h < kCw / 32; ++h) {  // 32-column halves (f16: two per chunk)
+              const int cc = c0 + 32 * h;
+              float v[32];
+              if (e.nkb > 0) {
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + cc), v);
+              } else {
+  #pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = 0.f;
+              }
+              if (!row_ok) {
+  #pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = 0.f;
+              }
+              const int ncol = max(0, min(32, e.cols - cc));
+              if (tma_out == kTmaStoreC && p.beta && row_ok) {
+                float c[32];
+                if (cin_tma) {
+                  if constexpr (!kF16) {
+  #pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                      const float4 t = *reinterpret_cast<const float4*>(row + ((u ^ (lane & 7)) * 16));
+                      c[4 * u] = t.x; c[4 * u + 1] = t.y; c[4 * u + 2] = t.z; c[4 * u + 3] = t.w;
+                    }
+                  } else {
+  #pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                      const uint4 t = *reinterpret_cast<const uint4*>(row + (((4 * h + u) ^ (lane & 7)) * 16));
+                      const uint32_t w4[4] = {t.x, t.y, t.z, t.w};
+  #pragma unroll
+                      for (int w = 0; w < 4; ++w) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[w]));
+                        c[8 * u + 2 * w] = f.x; c[8 * u + 2 * w + 1] = f.y;
+                      }
+                    }
+                  }
+                } else if (ncol > 0) {
+                  load_cin(cc, ncol, c);
+                } else {
+  #pragma unroll
+                  for (int i = 0; i < 32; ++i) c[i] = 0.f;
+                }
+  #pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += c[i];
+              }
+              if (tma_out == kTmaStoreC && p.ex.any) {
+  #pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (i < ncol) v[i] = apply_exprs(p.ex, v[i], (int64_t)e.n0 + cc + i);
+              }
+              if constexpr (!kF16) {
+  #pragma unroll
+                for (int u = 0; u < 8; ++u)
+                  *reinterpret_cast<float4*>(row + ((u ^ (lane & 7)) * 16)) =
+                      make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+              } else {
+  #pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  uint32_t w4[4];
+  #pragma unroll
+                  for (int w = 0; w < 4; ++w) {
+                    const __half2 hv = __floats2half2_rn(v[8 * u + 2 * w], v[8 * u + 2 * w + 1]);
+                    w4[w] = *reinterpret_cast<const uint32_t*>(&hv);
+                  }
+                  *reinterpret_cast<uint4*>(row + (((4 * h + u) ^ (lane & 7)) * 16)) =
+                      make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                }
+              }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (tma_out == kTmaStoreC) tma_store_2d(&tmC, smem_addr(buf), (int32_t)gcol, y0);
+              else if (tma_out == kTmaReduceC) tma_reduce_add_2d(&tmC, smem_addr(buf), (int32_t)gcol, y0);
+              else tma_store_3d(&tmC, smem_addr(buf), (int32_t)gcol, y0, e.part);
+              bulk_commit_group();
+            }
+            ++epi_slot;
+          }
+          return true;
+        };
+        const bool chunks_ok = (sizeof(OutT) == 2 && tma_out == kTmaStoreC)
+                                   ? chunks(std::integral_constant<bool, true>())
+                                   : chunks(std::integral_constant<bool, false>());
+        if (!chunks_ok) break;
+        if (wide) {
+          // the ring is refilled only by a next item, which a wide CTA has
+          // not; still, the stores must read their buffers before the CTA ends
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+        }
+      } else
       for (int c0 = 0; c0 < e.cols; c0 += 32) {
         float v[32];
         if (e.nkb > 0) {
@@ -675,48 +837,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int ncol = min(32, e.cols - c0);
         const int64_t gcol = (int64_t)e.n0 + c0;
-        if (tma_out != kTmaNone) {
-          // TMA path (program tile == hardware tile). Stage [32 rows × 32
-          // cols] in 128-byte-swizzled shared memory (row r's 16-byte chunk j
-          // at chunk j ^ (r % 8): the warp's float4 writes are bank-conflict
-          // free) and let TMA write, reduce-add or store it; rows/columns past
-          // M/N are clipped by TMA, so rows past M carry zeros.
-          if (!row_ok) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
-          }
-          if (tma_out == kTmaStoreC && p.beta && row_ok) {
-            float c[32];
-            load_cin(c0, ncol, c);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] += c[i];
-          }
-          if (tma_out == kTmaStoreC && p.ex.any) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < ncol) v[i] = apply_exprs(p.ex, v[i], gcol + i);
-          }
-          uint8_t* buf = epi_buf + (size_t)(epi_slot & 1) * Cf::kEpiBufBytes;
-          // The bulk op issued two chunks ago must have finished reading buf.
-          if (lane == 0) bulk_wait_group_read<1>();
-          __syncwarp();
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4* q4 = reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16));
-            *q4 = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            const int32_t y = (int32_t)(grow - lane);
-            if (tma_out == kTmaStoreC) tma_store_2d(&tmC, smem_addr(buf), (int32_t)gcol, y);
-            else if (tma_out == kTmaReduceC) tma_reduce_add_2d(&tmC, smem_addr(buf), (int32_t)gcol, y);
-            else tma_store_3d(&tmC, smem_addr(buf), (int32_t)gcol, y, e.part);
-            bulk_commit_group();
-          }
-          ++epi_slot;
-          continue;
-        }
         if (!row_ok) continue;
         if (p.epilogue == kEpiStore) {
           OutT* dst = reinterpret_cast<OutT*>(p.C) + grow * p.ldc + gcol;
@@ -833,17 +953,11 @@ __global__ void __launch_bounds__(128, 1)
     mbar_init(smem_addr(done), 1);
     fence_mbar_init();
   }
-  if (warp == 0) {
-    tmem_alloc(smem_addr(tmem_holder), BN);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_holder;
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const uint32_t idesc = idesc_f16_f32(128, BN, 0, 1);
   uint32_t phase = 0;
+  uint32_t tmem_base = 0;
+  bool have_tmem = false;
   for (int32_t pos = blockIdx.x; pos < p.positions; pos += gridDim.x) {
     const Extent e = program_extent<128, BN>(p, pos, kSmallK);
     const int kvalid = e.nkb > 0 ? e.k_end - e.k_begin : 0;  // <= kSmallK (plan rule)
@@ -886,9 +1000,20 @@ __global__ void __launch_bounds__(128, 1)
       for (int off = 0; off < bytes; off += 16)
         cp_async_16(smem_addr(cin_row + off), src + off, (uint32_t)min(16, bytes - off));
     }
+    if (!have_tmem && warp == 0) {
+      // first item: the TMEM allocation (~0.35 µs) overlaps the copies in flight
+      tmem_alloc(smem_addr(tmem_holder), BN);
+      tmem_relinquish();
+    }
     cp_async_wait_all();
     fence_proxy_async_smem();  // cp.async wrote through the generic proxy; the MMA reads via async
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    if (!have_tmem) {
+      tmem_base = *tmem_holder;
+      have_tmem = true;
+    }
     if (t == 0 && k16 > 0) {
       tc_fence_after();
       const uint64_t da0 = smem_desc_sw128(smem_addr(sA), 16, 1024);
@@ -974,7 +1099,7 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     tc_fence_after();
   }
-  if (warp == 0) tmem_dealloc(tmem_base, BN);
+  if (have_tmem && warp == 0) tmem_dealloc(tmem_base, BN);
 }
 
 // C = beta·C_in + Σ_s ws[s] in a fixed order (split_k_serial): deterministic.
@@ -1390,7 +1515,8 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   kp.vec_c = aligned16(Cp) && ((ldc * (int64_t)out_bytes) % 16 == 0) &&
              ((d.block_n * (int64_t)out_bytes) % 16 == 0);
   kp.vec_ws = (d.n % 4 == 0) && (d.block_n % 4 == 0) && aligned16(workspace);
-  kp.cin_smem = plan->positions <= plan->grid / plan->ctas_per_tile && kp.vec_c;
+  kp.one_item = plan->positions <= plan->grid / plan->ctas_per_tile ? 1 : 0;
+  kp.cin_smem = kp.one_item && kp.vec_c;
   kp.C = Cp;
   kp.ldc = ldc;
   kp.ws = reinterpret_cast<float*>(workspace);
@@ -1415,6 +1541,8 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
     if (plan->epilogue == kEpiStore) kp.tma_out = kTmaStoreC;
     if (plan->epilogue == kEpiAtomic) kp.tma_out = kTmaReduceC;
   }
+  if (exact_hw_tile && d.c_dtype == TB_F16 && aligned16(Cp) && ldc % 8 == 0 && plan->epilogue == kEpiStore)
+    kp.tma_out = kTmaStoreC;  // f16 C: [32 rows × 64 columns] boxes
   if (exact_hw_tile && plan->epilogue == kEpiWorkspace && aligned16(workspace) && d.n % 4 == 0)
     kp.tma_out = kTmaStoreWs;
   // The tail's K pieces reduce-add f32 partial tiles through the same C
@@ -1432,6 +1560,12 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
       cuuint64_t dims[3] = {(cuuint64_t)d.n, (cuuint64_t)d.m, (cuuint64_t)kp.map.split_k};
       cuuint64_t strides[2] = {(cuuint64_t)d.n * 4, (cuuint64_t)d.m * (cuuint64_t)d.n * 4};
       r = encode_cached(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, workspace, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+    } else if (d.c_dtype == TB_F16) {
+      cuuint64_t dims[2] = {(cuuint64_t)d.n, (cuuint64_t)d.m};
+      cuuint64_t strides[1] = {(cuuint64_t)ldc * 2};
+      cuuint32_t box16[2] = {64, 32};
+      r = encode_cached(&tcm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Cp, dims, strides, box16,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE);
     } else {
       cuuint64_t dims[2] = {(cuuint64_t)d.n, (cuuint64_t)d.m};

@@ -107,19 +107,18 @@ def test_large_program_tiles_run_as_subtiles(bm, bn, tile, sub):
 
 
 def test_tail_split_plan_facts():
-    """8192 x 1024 x 8192 (one rank of an 8-way N-shard): 128 pair items on
-    74 CTA pairs leave the second wave 73 % full; the plan cuts every item
-    into K pieces. f16 C, beta = 0 and deterministic plans keep whole items."""
-    p = plan(8192, 1024, 8192, 256, 256, 64)
+    """8192 x 2048 x 8192 (one rank of a 4-way N-shard): 256 pair items on
+    74 CTA pairs; two whole waves, then the last 108 items in two K pieces.
+    f16 C, beta = 0, split-K and deterministic plans keep whole items, and
+    so does the 8-way slice (128 items), where pieces measured slower."""
+    p = plan(8192, 2048, 8192, 256, 256, 64)
     ts = p.info["tail_split"]
-    assert ts is not None and ts["whole_items"] + ts["split_items"] == p.info["work_items"] == 128
-    assert ts["k_pieces"] >= 2
-    assert p.info["walk_positions"] == ts["whole_items"] + ts["split_items"] * ts["k_pieces"]
-    assert p.info["grid"] == 148
+    assert ts == {"whole_items": 148, "split_items": 108, "k_pieces": 2}
+    assert p.info["walk_positions"] == 148 + 108 * 2 and p.info["grid"] == 148
     for kw in (dict(c_dtype="f16"), dict(beta=0), dict(deterministic=True), dict(split_k=2)):
-        q = plan(8192, 1024, 8192, 256, 256, 64, **kw)
+        q = plan(8192, 2048, 8192, 256, 256, 64, **kw)
         assert q.info["tail_split"] is None, kw
-    # 8192^3 (1024 items, 13.8 waves) gains too little to split
+    assert plan(8192, 1024, 8192, 256, 256, 64).info["tail_split"] is None
     assert plan(8192, 8192, 8192, 256, 256, 64).info["tail_split"] is None
 
 

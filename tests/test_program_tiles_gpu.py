@@ -64,8 +64,8 @@ def test_large_program_tiles(cuda, shape, knobs, sub, out):
     assert float(np.abs(got - ref).max()) <= tol
 
 
-@pytest.mark.parametrize("shape,tile", [((4096, 2560, 2048), (256, 256)), ((2304, 4352, 2048), (256, 256)),
-                                        ((4096, 2560, 2048), (128, 128)), ((2560, 4096, 1536), (256, 128))],
+@pytest.mark.parametrize("shape,tile", [((4096, 2560, 8192), (256, 256)), ((2304, 4352, 8192), (256, 256)),
+                                        ((4096, 2560, 8192), (128, 128)), ((2560, 4096, 8192), (256, 128))],
                          ids=["pair", "pair_ragged_m", "fused_128", "fused_256x128"])
 @pytest.mark.parametrize("persistent", [False, True])
 def test_tail_split_matches_oracle_and_whole_items(cuda, shape, tile, persistent):
@@ -106,7 +106,7 @@ def test_tail_split_falls_back_when_c_is_not_tma_addressable(cuda):
     import torch
     import mini_triton_nvgpu_v1_b200 as tb
     import oracle
-    m, n, k = 4096, 2560, 2048
+    m, n, k = 4096, 2560, 8192
     tA, tB, _ = _inputs(cuda, m, n, k, 44)
     big = torch.randn(m, n + 1, device=cuda)
     tC = big[:, :n]
@@ -137,8 +137,8 @@ def test_nshard_entry_rank_by_rank(cuda, world, slices):
         if nc == 0:
             continue
         if slices == "own":
-            b = tB[:, c0:c0 + nc].contiguous()
-            c = tCin[:, c0:c0 + nc].contiguous()
+            b = tB[:, c0:c0 + nc].clone()
+            c = tCin[:, c0:c0 + nc].clone()
             sh.run(tA, b, c)
             full[:, c0:c0 + nc] = c
         else:
