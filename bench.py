@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kshard", action="store_true",
+                    help="gemm8192 at N>1: skip the extra K-sharded split-K measurement")
     ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "splitk", "sweep"],
                     help="gemm8192: the headline 8192^3 N-sharded GEMM; splitk: the skinny "
                          "512x512x65536 split-K config (K-sharded + reduce-scatter at N>1)")
@@ -274,6 +276,15 @@ def run_reference(args):
 BURST_REGION_S = 0.5  # timed regions shorter than this are compared with the burst peak
 
 
+def roofline_denominator(region_s: float, peak_burst: float, peak_sustained):
+    """(peak, is_burst): the measured cuBLAS burst figure for a timed region
+    shorter than BURST_REGION_S (a kernel timed nearly alone, before the
+    power cap settles the clock), the sustained figure for longer ones."""
+    if region_s < BURST_REGION_S or peak_sustained is None:
+        return peak_burst, True
+    return peak_sustained, False
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -404,12 +415,23 @@ def run_ours(args):
         dist.all_reduce(h2d)
         dist.all_reduce(d2h)
 
+    # At N > 1 the skinny split-K config runs K-sharded as well, so a scaling
+    # run records the fused reduce-scatter (and NCCL's, for comparison).
+    kshard = None
+    if world > 1 and not args.no_kshard:
+        kshard = {}
+        for mode in ("peer", "nccl"):
+            try:
+                r = splitk_measure(mode, 50, 5)
+                kshard[mode] = {"workload": r["workload"], "ms_per_step": round(r["ms_per_step"], 5),
+                                "tflops": round(r["tflops"], 2), "hbm_frac_per_gpu": round(r["gbs_per_gpu"] / r["hbm"], 4)}
+            except Exception as exc:  # report, do not lose the headline line
+                kshard[mode] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
     if rank == 0:
         peak, peak_sus, peak_src = peaks()
         achieved = flops_rank / (ms_step * 1e-3) / 1e12  # rank 0's kernel: one launch per step
         region_s = ms_max * 1e-3
-        burst = region_s < BURST_REGION_S or peak_sus is None
-        denom = peak if burst else peak_sus
+        denom, burst = roofline_denominator(region_s, peak, peak_sus)
         kern = info["kernel"]
         cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline_block()
         alg_bytes = 2 * (M * K + K * ncols) + 8 * M * ncols
@@ -448,6 +470,8 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }
+        if kshard is not None:
+            out["kshard_splitk_512x512x65536"] = kshard
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()
@@ -461,27 +485,26 @@ SK_SPLIT = 16
 SK_BLOCK = dict(block_m=256, block_n=256, block_k=64, num_warps=4, num_stages=4)
 
 
-def run_splitk(args):
-    """512 x 512 x 65536 with split_k = 16 (split_k_serial: f32 workspace +
-    ordered reduction). At N > 1 the K dimension is sharded across ranks and
-    the f32 partials are combined by an NCCL reduce-scatter (rank r keeps
-    rows [r·512/N, (r+1)·512/N)). Reported against the HBM roofline."""
+def splitk_measure(mode: str, steps: int, warmup: int):
+    """Times 512 x 512 x 65536 split-K on this process's GPU (the process
+    group, if any, is already up). mode: "local" (1 GPU, split_k_serial), or
+    at N > 1 with K sharded across ranks: "peer" (reduce-scatter fused into
+    the GEMM over NVLink, tb_matmul_run_kshard_peer), "capi"
+    (tb_matmul_run_kshard_nccl) or "nccl" (torch.distributed reduce-scatter
+    after the GEMM). Returns the line's measured fields (max over ranks)."""
     import torch
     import torch.distributed as dist
     import mini_triton_nvgpu_v1_b200 as tb
     from mini_triton_nvgpu_v1_b200 import parallel as par
 
     rank, world, local = dist_env()
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream(dev)
     k0, kr = par.k_shard(SK_K, world, rank, SK_BLOCK["block_k"])
     g = torch.Generator(device=dev).manual_seed(6)
     A = (torch.rand(SK_M, SK_K, device=dev, generator=g) * 2 - 1).half()[:, k0:k0 + kr].contiguous()
     B = (torch.rand(SK_K, SK_N, device=dev, generator=g) * 2 - 1).half()[k0:k0 + kr].contiguous()
-    peer = world > 1 and args.kshard == "peer"
+    peer, capi = mode == "peer", mode == "capi"
     split_local = SK_SPLIT if peer else max(1, SK_SPLIT // world)
     cfg = tb.KernelConfig(m=SK_M, n=SK_N, k=kr, split_k=split_local,
                           reduction_mode="split_k_parallel" if peer else "split_k_serial", **SK_BLOCK)
@@ -491,12 +514,11 @@ def run_splitk(args):
     C_rows = torch.zeros(mr, SK_N, device=dev)
     partial = torch.zeros(SK_M, SK_N, device=dev)
     recv = torch.empty_like(C_rows)
-    capi = world > 1 and args.kshard == "capi"
     comm = par.PeerKShard(C_rows) if peer else None
     ncomm = par.NcclKShard(C_rows) if capi else None
 
     def step():
-        if world == 1:
+        if mode == "local":
             plan.run_ptr(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), C_rows.data_ptr(),
                          SK_N, ws.data_ptr(), ws.numel(), stream.cuda_stream)
         elif peer:
@@ -515,43 +537,63 @@ def run_splitk(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, warmup)):
         step()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     ev1.record(stream)
     barrier()
     t = torch.tensor([ev0.elapsed_time(ev1)], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_step = float(t.item()) / args.steps
-    flops = 2.0 * SK_M * SK_N * SK_K
-    bytes_alg = 2.0 * (SK_M * SK_K + SK_K * SK_N) + 8.0 * SK_M * SK_N
-    if rank == 0:
-        hbm = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("hbm_gbs", 6650.0) \
-            if (ROOT / "MEASURED_PEAKS.json").exists() else 6650.0
-        gbs = bytes_alg / world / (ms_step * 1e-3) / 1e9
-        print(json.dumps({
-            "metric": "GEMM TFLOP/s, 512x512x65536 split-K (HBM-roofline config)",
-            "value": round(flops / (ms_step * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "strong", "dtype": "f16", "data": "synthetic",
-            "config": {"workload": f"tb.matmul {SK_M}x{SK_N}x{SK_K} split_k={SK_SPLIT} "
-                                   f"({('K-shard x%d, reduce-scatter fused into the GEMM over NVLink' if peer else 'K-shard x%d, tb_matmul_run_kshard_nccl' if capi else 'K-shard x%d + NCCL reduce-scatter') % world if world > 1 else '1 GPU'})",
-                       "split_k_per_rank": split_local, "kernel": plan.info["kernel"]},
-            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(gbs / hbm, 4),
-                         "note": "algorithmic bytes per GPU (its A/B K-slice + C_in + C) / step time"},
-            "gpu_launches": args.steps * (2 if world == 1 else 3 if peer else 2),
-        }), flush=True)
+    ms_step = float(t.item()) / steps
     if comm is not None:
         comm.check()
         comm.close()
     if ncomm is not None:
         ncomm.close()
+    flops = 2.0 * SK_M * SK_N * SK_K
+    bytes_alg = 2.0 * (SK_M * SK_K + SK_K * SK_N) + 8.0 * SK_M * SK_N
+    hbm = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("hbm_gbs", 6650.0) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 6650.0
+    gbs = bytes_alg / world / (ms_step * 1e-3) / 1e9
+    what = {"local": "1 GPU", "peer": f"K-shard x{world}, reduce-scatter fused into the GEMM over NVLink",
+            "capi": f"K-shard x{world}, tb_matmul_run_kshard_nccl",
+            "nccl": f"K-shard x{world} + NCCL reduce-scatter"}[mode]
+    return {"ms_per_step": ms_step, "tflops": flops / (ms_step * 1e-3) / 1e12, "gbs_per_gpu": gbs, "hbm": hbm,
+            "workload": f"tb.matmul {SK_M}x{SK_N}x{SK_K} split_k={SK_SPLIT} ({what})",
+            "split_k_per_rank": split_local, "kernel": plan.info["kernel"],
+            "launches_per_step": 2 if mode == "local" else 3 if peer else 2}
+
+
+def run_splitk(args):
+    """512 x 512 x 65536 with split_k = 16 (split_k_serial: f32 workspace +
+    ordered reduction). At N > 1 the K dimension is sharded across ranks and
+    the f32 partials are combined by a reduce-scatter (rank r keeps rows
+    [r·512/N, (r+1)·512/N)). Reported against the HBM roofline."""
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    r = splitk_measure("local" if world == 1 else args.kshard, args.steps, args.warmup)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "GEMM TFLOP/s, 512x512x65536 split-K (HBM-roofline config)",
+            "value": round(r["tflops"], 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(r["ms_per_step"], 5),
+            "higher_is_better": True, "scaling": "strong", "dtype": "f16", "data": "synthetic",
+            "config": {"workload": r["workload"], "split_k_per_rank": r["split_k_per_rank"],
+                       "kernel": r["kernel"]},
+            "roofline": {"bound": "hbm", "achieved": round(r["gbs_per_gpu"], 1), "peak": r["hbm"], "unit": "GB/s",
+                         "frac": round(r["gbs_per_gpu"] / r["hbm"], 4),
+                         "note": "algorithmic bytes per GPU (its A/B K-slice + C_in + C) / step time"},
+            "gpu_launches": args.steps * r["launches_per_step"],
+        }), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

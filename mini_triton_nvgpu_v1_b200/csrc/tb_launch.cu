@@ -201,8 +201,10 @@ struct Extent {
 // Work of walk position `pos` on a HM × HN hardware tile: its rows and
 // columns inside the problem (clipped to its program tile) and its K range;
 // nkb counts ring fills of kb K elements.
+__host__ __device__ __forceinline__ int32_t imin(int32_t a, int32_t b) { return a < b ? a : b; }
+
 template <int HM, int HN>
-__device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pos, int32_t kb) {
+__host__ __device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pos, int32_t kb) {
   int32_t w = pos;
   int32_t piece = -1;
   if (pos >= p.dp_items) {
@@ -220,21 +222,21 @@ __device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pos, 
   const int32_t sm = (sub / p.sub_n) * HM, sn = (sub % p.sub_n) * HN;
   e.m0 = wk.tile_m * p.block_m + sm;
   e.n0 = wk.tile_n * p.block_n + sn;
-  e.rows = min(p.block_m * (p.fuse == 1 || p.fuse == 4 ? 2 : 1) - sm, p.M - e.m0);
-  e.cols = min(p.block_n * (p.fuse >= 2 ? 2 : 1) - sn, p.N - e.n0);
+  e.rows = imin(p.block_m * (p.fuse == 1 || p.fuse == 4 ? 2 : 1) - sm, p.M - e.m0);
+  e.cols = imin(p.block_n * (p.fuse >= 2 ? 2 : 1) - sn, p.N - e.n0);
   if (nsub > 1) {
-    e.rows = min(e.rows, HM);
-    e.cols = min(e.cols, HN);
+    e.rows = imin(e.rows, HM);
+    e.cols = imin(e.cols, HN);
   }
   e.k_begin = wk.kt_begin * p.block_k;
-  e.k_end = min(p.K, (wk.kt_begin + wk.kt_count) * p.block_k);
+  e.k_end = imin(p.K, (wk.kt_begin + wk.kt_count) * p.block_k);
   e.nkb = e.k_end > e.k_begin && e.rows > 0 && e.cols > 0 ? (e.k_end - e.k_begin + kb - 1) / kb : 0;
   e.part = wk.part;
   e.piece = piece >= 0;
   if (piece >= 0) {
     const int32_t f0 = (int32_t)((int64_t)e.nkb * piece / p.tail_parts);
     const int32_t f1 = (int32_t)((int64_t)e.nkb * (piece + 1) / p.tail_parts);
-    e.k_end = min(e.k_end, e.k_begin + f1 * kb);
+    e.k_end = imin(e.k_end, e.k_begin + f1 * kb);
     e.k_begin += f0 * kb;
     e.nkb = f1 - f0;
   }
@@ -724,6 +726,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             cin_phase ^= 1u;
             if (!okc) return false;
           }
+          // C_in through the rotating buffers: the boxes of the later chunks
+          // are prefetched into L2 now, and each 32-column half's loads are
+          // issued one half ahead of its use (a DRAM round trip per chunk
+          // otherwise serialises the epilogue).
+          const bool pipe_cin = !cin_tma && tma_out == kTmaStoreC && p.beta && row_ok && !cin_from_smem;
+          if (!cin_tma && tma_out == kTmaStoreC && p.beta && !cin_from_smem && lane == 0)
+            for (int j = 1; j < nch; ++j) tma_prefetch_l2_2d(&tmC, (int32_t)(e.n0 + j * kCw), y0);
+          auto fetch_cin = [&](int cc, float (&c)[32]) {
+            const int nc = max(0, min(32, e.cols - cc));
+            if (nc > 0) {
+              load_cin(cc, nc, c);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) c[i] = 0.f;
+            }
+          };
+          float cn[32];
+          if (pipe_cin) fetch_cin(0, cn);
           for (int j = 0; j < nch; ++j) {
             const int c0 = j * kCw;
             const int64_t gcol = (int64_t)e.n0 + c0;
@@ -735,18 +755,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
             }
             uint8_t* row = buf + lane * 128;
-  #pragma unroll
+#pragma unroll
             for (int h = 0; h < kCw / 32; ++h) {  // 32-column halves (f16: two per chunk)
               const int cc = c0 + 32 * h;
               float v[32];
               if (e.nkb > 0) {
                 tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + cc), v);
               } else {
-  #pragma unroll
+#pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = 0.f;
               }
               if (!row_ok) {
-  #pragma unroll
+#pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = 0.f;
               }
               const int ncol = max(0, min(32, e.cols - cc));
@@ -754,47 +774,51 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float c[32];
                 if (cin_tma) {
                   if constexpr (!kF16) {
-  #pragma unroll
+#pragma unroll
                     for (int u = 0; u < 8; ++u) {
                       const float4 t = *reinterpret_cast<const float4*>(row + ((u ^ (lane & 7)) * 16));
                       c[4 * u] = t.x; c[4 * u + 1] = t.y; c[4 * u + 2] = t.z; c[4 * u + 3] = t.w;
                     }
                   } else {
-  #pragma unroll
+#pragma unroll
                     for (int u = 0; u < 4; ++u) {
                       const uint4 t = *reinterpret_cast<const uint4*>(row + (((4 * h + u) ^ (lane & 7)) * 16));
                       const uint32_t w4[4] = {t.x, t.y, t.z, t.w};
-  #pragma unroll
+#pragma unroll
                       for (int w = 0; w < 4; ++w) {
                         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[w]));
                         c[8 * u + 2 * w] = f.x; c[8 * u + 2 * w + 1] = f.y;
                       }
                     }
                   }
+                } else if (pipe_cin) {
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) c[i] = cn[i];
+                  if (cc + 32 < nch * kCw) fetch_cin(cc + 32, cn);
                 } else if (ncol > 0) {
                   load_cin(cc, ncol, c);
                 } else {
-  #pragma unroll
+#pragma unroll
                   for (int i = 0; i < 32; ++i) c[i] = 0.f;
                 }
-  #pragma unroll
+#pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] += c[i];
               }
               if (tma_out == kTmaStoreC && p.ex.any) {
-  #pragma unroll
+#pragma unroll
                 for (int i = 0; i < 32; ++i)
                   if (i < ncol) v[i] = apply_exprs(p.ex, v[i], (int64_t)e.n0 + cc + i);
               }
               if constexpr (!kF16) {
-  #pragma unroll
+#pragma unroll
                 for (int u = 0; u < 8; ++u)
                   *reinterpret_cast<float4*>(row + ((u ^ (lane & 7)) * 16)) =
                       make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
               } else {
-  #pragma unroll
+#pragma unroll
                 for (int u = 0; u < 4; ++u) {
                   uint32_t w4[4];
-  #pragma unroll
+#pragma unroll
                   for (int w = 0; w < 4; ++w) {
                     const __half2 hv = __floats2half2_rn(v[8 * u + 2 * w], v[8 * u + 2 * w + 1]);
                     w4[w] = *reinterpret_cast<const uint32_t*>(&hv);
@@ -923,6 +947,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // its accumulator row from TMEM and stores it. A CTA walks several items in
 // turn when there are more items than CTAs (persistent plans).
 constexpr int kSmallK = 128;
+// Work of the first kSmallTab walk positions, derived on the host (the same
+// program_extent): a single thread's chain of mapping arithmetic and
+// parameter reads took ~0.6 µs of a ~4 µs kernel.
+constexpr int kSmallTab = 64;
+struct SmallTab {
+  int32_t n;  // positions described (0: derive on the device)
+  int32_t m0[kSmallTab], n0[kSmallTab], k_begin[kSmallTab];
+  int16_t rows[kSmallTab], cols[kSmallTab], kvalid[kSmallTab], part[kSmallTab];
+};
 constexpr uint32_t kSmallASub = 128 * 64 * 2;         // one [128 m × 64 k] K-major sub-tile
 constexpr uint32_t kSmallABytes = kSmallK / 64 * kSmallASub;
 constexpr uint32_t kSmallBox = kSmallK * 64 * 2;      // one [kSmallK k × 64 n] MN-major box
@@ -931,14 +964,26 @@ template <int BN, typename OutT>
 struct SmallCfg {
   static constexpr uint32_t kBBytes = BN / 64 * kSmallBox;
   static constexpr uint32_t kCinStride = BN * sizeof(OutT) + 16;  // padded row: conflict-free reads
-  static constexpr size_t kSmem = 1024 + kSmallABytes + kBBytes + 128 * kCinStride + 64;
+  static constexpr size_t kSmem = 1024 + kSmallABytes + kBBytes + 128 * kCinStride + 64 + 16;
 };
 
 template <int BN, typename OutT>
 __global__ void __launch_bounds__(128, 1)
-    tb_gemm_small_kernel(const KParams p, const uint16_t* __restrict__ A, int64_t lda,
-                         const uint16_t* __restrict__ B, int64_t ldb) {
+    tb_gemm_small_kernel(const __grid_constant__ KParams pk, const __grid_constant__ SmallTab tab,
+                         const uint16_t* __restrict__ A, int64_t lda, const uint16_t* __restrict__ B,
+                         int64_t ldb) {
   using Sc = SmallCfg<BN, OutT>;
+  // The parameters come through the constant bank, which each launch
+  // refills: reading them field by field inside the dependent mapping
+  // arithmetic costs a miss per cache line in series (~0.6 µs measured).
+  // One word per thread brings every line in at once; the kernel then reads
+  // its shared-memory copy.
+  static_assert(sizeof(KParams) % 4 == 0 && sizeof(KParams) <= 4 * 128, "KParams copy");
+  __shared__ __align__(16) KParams p_s;
+  if (threadIdx.x < sizeof(KParams) / 4)
+    reinterpret_cast<uint32_t*>(&p_s)[threadIdx.x] = reinterpret_cast<const uint32_t*>(&pk)[threadIdx.x];
+  __syncthreads();
+  const KParams& p = p_s;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -959,35 +1004,45 @@ __global__ void __launch_bounds__(128, 1)
   uint32_t tmem_base = 0;
   bool have_tmem = false;
   for (int32_t pos = blockIdx.x; pos < p.positions; pos += gridDim.x) {
-    const Extent e = program_extent<128, BN>(p, pos, kSmallK);
-    const int kvalid = e.nkb > 0 ? e.k_end - e.k_begin : 0;  // <= kSmallK (plan rule)
-    const int k16 = (kvalid + 15) / 16 * 16;                 // K covered by the MMA steps
-    // ---- stage A (K-major, two [128 × 64] sub-tiles) and B (MN-major
-    //      [kSmallK × 64] boxes), 16-byte chunks, zero past K / M / N
-    for (int c = t; c < 128 * (k16 / 8); c += 128) {
-      const int r = c / (k16 / 8), kc = c % (k16 / 8);   // row, 8-element K chunk
-      const int k = kc * 8;
-      const int64_t gm = (int64_t)e.m0 + r;
-      uint32_t bytes = 0;
-      const uint16_t* src = A;
-      if (gm < p.M && k < kvalid) {
-        bytes = (uint32_t)min(16, (kvalid - k) * 2);
-        src = A + gm * lda + e.k_begin + k;
-      }
-      const uint32_t dst = smem_addr(sA + (k / 64) * kSmallASub + r * 128 + (((k / 8) % 8) ^ (r % 8)) * 16);
-      cp_async_16(dst, src, bytes);
+    Extent e;
+    int kvalid;
+    if (pos < tab.n) {
+      e.m0 = tab.m0[pos];
+      e.n0 = tab.n0[pos];
+      e.k_begin = tab.k_begin[pos];
+      e.rows = tab.rows[pos];
+      e.cols = tab.cols[pos];
+      e.part = tab.part[pos];
+      kvalid = tab.kvalid[pos];
+    } else {
+      e = program_extent<128, BN>(p, pos, kSmallK);
+      kvalid = e.nkb > 0 ? e.k_end - e.k_begin : 0;  // <= kSmallK (plan rule)
     }
-    for (int c = t; c < k16 * (BN / 8); c += 128) {
-      const int kr = c / (BN / 8), nc = c % (BN / 8);    // K row, 8-column chunk
-      const int64_t gn = (int64_t)e.n0 + nc * 8;
-      uint32_t bytes = 0;
-      const uint16_t* src = B;
-      if (kr < kvalid && gn < p.N) {
-        bytes = (uint32_t)(p.N - gn >= 8 ? 16 : (p.N - gn) * 2);
-        src = B + (int64_t)(e.k_begin + kr) * ldb + gn;
+    const int k16 = (kvalid + 15) / 16 * 16;                 // K covered by the MMA steps
+    // ---- stage A (K-major, two [128 × 64] sub-tiles; thread t copies row t)
+    //      and B (MN-major [kSmallK × 64] boxes; thread t < k16 copies K row
+    //      t), 16-byte chunks, zero past K / M / N
+    {
+      const int64_t gm = (int64_t)e.m0 + t;
+      const uint16_t* arow = A + gm * lda + e.k_begin;
+      uint8_t* drow = sA + t * 128;
+      for (int k = 0; k < k16; k += 8) {
+        const uint32_t bytes = gm < p.M && k < kvalid ? (uint32_t)min(16, (kvalid - k) * 2) : 0u;
+        cp_async_16(smem_addr(drow + (k / 64) * kSmallASub + (((k / 8) % 8) ^ (t % 8)) * 16),
+                    bytes ? arow + k : A, bytes);
       }
-      const uint32_t dst = smem_addr(sB + (nc / 8) * kSmallBox + kr * 128 + ((nc % 8) ^ (kr % 8)) * 16);
-      cp_async_16(dst, src, bytes);
+    }
+    if (t < k16) {
+      const uint16_t* brow = B + (int64_t)(e.k_begin + t) * ldb + e.n0;
+      uint8_t* drow = sB + t * 128;
+#pragma unroll
+      for (int nc = 0; nc < BN / 8; ++nc) {
+        const int64_t gn = (int64_t)e.n0 + nc * 8;
+        const uint32_t bytes =
+            t < kvalid && gn < p.N ? (uint32_t)(p.N - gn >= 8 ? 16 : (p.N - gn) * 2) : 0u;
+        cp_async_16(smem_addr(drow + (nc / 8) * kSmallBox + ((nc % 8) ^ (t % 8)) * 16),
+                    bytes ? brow + nc * 8 : B, bytes);
+      }
     }
     // ---- this thread's C_in row, fetched alongside the operands
     const bool row_ok = t < e.rows;
@@ -1329,7 +1384,20 @@ tbStatus launch_small_bn(const tb_matmul_plan* plan, const KParams& kp, const vo
       return tb_fail(TB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     if (dev >= 0 && dev < kMaxDevices) g_small_attr_set[bi][ot][dev].store(true);
   }
-  kern<<<(unsigned)plan->grid, 128, smem, stream>>>(kp, static_cast<const uint16_t*>(A), lda,
+  SmallTab tab;
+  std::memset(&tab, 0, sizeof(tab));
+  tab.n = kp.positions <= kSmallTab ? kp.positions : 0;
+  for (int32_t pos = 0; pos < tab.n; ++pos) {
+    const Extent e = program_extent<128, BN>(kp, pos, kSmallK);
+    tab.m0[pos] = e.m0;
+    tab.n0[pos] = e.n0;
+    tab.k_begin[pos] = e.k_begin;
+    tab.rows[pos] = (int16_t)std::max(-1, std::min(e.rows, 32767));
+    tab.cols[pos] = (int16_t)std::max(-1, std::min(e.cols, 32767));
+    tab.kvalid[pos] = (int16_t)(e.nkb > 0 ? e.k_end - e.k_begin : 0);
+    tab.part[pos] = (int16_t)e.part;
+  }
+  kern<<<(unsigned)plan->grid, 128, smem, stream>>>(kp, tab, static_cast<const uint16_t*>(A), lda,
                                                     static_cast<const uint16_t*>(B), ldb);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)

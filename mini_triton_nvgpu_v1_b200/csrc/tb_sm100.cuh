@@ -91,6 +91,14 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
+// Prefetch one box of a 2-D tensor into L2 (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // 2-D tiled store of one shared-memory box to global memory (bulk group).
 // Elements outside the tensor are not written.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x,

@@ -21,3 +21,13 @@ def test_reference_arm_json_line():
     assert line["impl"] == "reference" and line["value"] > 0 and line["gpu_launches"] == 0
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["config"]["m"] == 8192
+
+
+def test_roofline_denominator_follows_the_timed_region():
+    """20 steps of 8192^3 (~16 ms) compare with the burst peak, a ~1 s loop
+    with the sustained one (the power cap has settled the clock by then)."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    assert bench.roofline_denominator(0.016, 1655.2, 1386.1) == (1655.2, True)
+    assert bench.roofline_denominator(0.9, 1655.2, 1386.1) == (1386.1, False)
+    assert bench.roofline_denominator(0.9, 1655.2, None) == (1655.2, True)
