@@ -145,12 +145,13 @@ struct KParams {
   int32_t one_item;  // every CTA (pair) runs at most one work item: the ring is idle in its epilogue
   int32_t walk_grouped;  // tb::WalkMode: the order resident CTAs take work items in
   int32_t work_items;    // hardware work items (programs × sub-tiles, or fused programs)
-  int32_t positions;     // walk positions: dp_items + tail_items · tail_parts
+  int32_t positions;     // walk positions: dp_items + tail_segs · tail_slots
   int32_t sub_m, sub_n;  // hardware tiles per program along M / N (programs larger than a tile)
-  // Tail balancing (tb::TailSplit): walk positions [0, dp_items) run whole
-  // work items; the last tail_items items are each cut into tail_parts
-  // K pieces that are reduce-added into C.
-  int32_t dp_items, tail_items, tail_parts;
+  // Stream-K tail (tb_choose_tail_split): positions [0, dp_items) run whole
+  // work items; the last tail_items items are one run of tail_items ·
+  // tail_fills ring fills cut into tail_slots equal ranges, the slot of
+  // position dp_items + s·tail_slots + q being q and s its segment.
+  int32_t dp_items, tail_items, tail_slots, tail_segs, tail_fills;
   EpiExprs ex;       // applied in kEpiStore (split_k_serial: in the reduction)
   int32_t a_mn;      // A stored M-major (column-major m × k): MN-major UMMA operand
   int32_t b_kmaj;    // B stored K-major (column-major k × n): K-major UMMA operand
@@ -195,7 +196,7 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
 
 struct Extent {
   int32_t m0, n0, rows, cols, k_begin, k_end, nkb, part;
-  bool piece;  // a K piece of a tail work item: its partial sum is reduce-added into C
+  bool piece;  // part of a tail work item (stream-K): its partial sum is reduce-added into C
 };
 
 // Work of walk position `pos` on a HM × HN hardware tile: its rows and
@@ -206,11 +207,18 @@ __host__ __device__ __forceinline__ int32_t imin(int32_t a, int32_t b) { return 
 template <int HM, int HN>
 __host__ __device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pos, int32_t kb) {
   int32_t w = pos;
-  int32_t piece = -1;
+  int32_t f0 = 0, f1 = -1;  // the position's fills of its item (stream-K tail), or all
   if (pos >= p.dp_items) {
     const int32_t t = pos - p.dp_items;
-    piece = t / p.tail_items;
-    w = p.dp_items + t % p.tail_items;
+    const int32_t seg = t / p.tail_slots, q = t % p.tail_slots;
+    const int64_t U = (int64_t)p.tail_items * p.tail_fills;
+    const int64_t u0 = (int64_t)q * U / p.tail_slots, u1 = (int64_t)(q + 1) * U / p.tail_slots;
+    const int32_t i = (int32_t)(u0 / p.tail_fills) + seg;
+    const int64_t b = (int64_t)i * p.tail_fills;
+    f0 = (int32_t)((u0 > b ? u0 : b) - b);
+    f1 = (int32_t)((u1 < b + p.tail_fills ? u1 : b + p.tail_fills) - b);
+    if (i >= p.tail_items) f1 = f0;  // past the run: an empty position
+    w = p.dp_items + (i < p.tail_items ? i : p.tail_items - 1);
   }
   const int32_t nsub = p.sub_m * p.sub_n;
   const int32_t sub = w % nsub;
@@ -232,10 +240,15 @@ __host__ __device__ __forceinline__ Extent program_extent(const KParams& p, int3
   e.k_end = imin(p.K, (wk.kt_begin + wk.kt_count) * p.block_k);
   e.nkb = e.k_end > e.k_begin && e.rows > 0 && e.cols > 0 ? (e.k_end - e.k_begin + kb - 1) / kb : 0;
   e.part = wk.part;
-  e.piece = piece >= 0;
-  if (piece >= 0) {
-    const int32_t f0 = (int32_t)((int64_t)e.nkb * piece / p.tail_parts);
-    const int32_t f1 = (int32_t)((int64_t)e.nkb * (piece + 1) / p.tail_parts);
+  e.piece = false;
+  if (f1 >= 0) {
+    if (f1 <= f0) {  // empty: no loads, no MMA, no stores
+      e.nkb = 0;
+      e.cols = 0;
+      return e;
+    }
+    // a partial segment adds its sum into C; a whole item stores as usual
+    e.piece = f1 - f0 < e.nkb;
     e.k_end = imin(e.k_end, e.k_begin + f1 * kb);
     e.k_begin += f0 * kb;
     e.nkb = f1 - f0;
@@ -1570,7 +1583,9 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   kp.sub_n = plan->sub_n;
   kp.dp_items = (int32_t)plan->dp_items;
   kp.tail_items = (int32_t)plan->tail_items;
-  kp.tail_parts = (int32_t)plan->tail_parts;
+  kp.tail_slots = (int32_t)std::max<int64_t>(1, plan->tail_slots);
+  kp.tail_segs = (int32_t)plan->tail_segs;
+  kp.tail_fills = (int32_t)std::max<int64_t>(1, plan->tail_fills);
   kp.positions = (int32_t)plan->positions;
   kp.a_mn = d.a_col_major ? 1 : 0;
   kp.b_kmaj = d.b_col_major ? 1 : 0;
@@ -1618,7 +1633,7 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   if (plan->tail_items && kp.tma_out != kTmaStoreC) {
     kp.dp_items = kp.work_items;
     kp.tail_items = 0;
-    kp.tail_parts = 1;
+    kp.tail_segs = 0;
     kp.positions = kp.work_items;
   }
   if (kp.tma_out != kTmaNone) {

@@ -72,34 +72,36 @@ bool derive_warp_grid(int64_t num_warps, int64_t bm, int64_t bn, int64_t* gm,
 }  // namespace
 
 void tb_choose_tail_split(int64_t items, int64_t slots, int64_t fills, int64_t* dp_items,
-                          int64_t* tail_items, int64_t* tail_parts) {
-  // Cost model in ring fills per slot (all items have `fills` fills): the
-  // whole waves before the tail keep their items whole; the remaining L
-  // items (one wave plus the partial one) are cut into s equal K pieces, each
-  // charged kPieceCost extra fills for its partial-tile reduce-add and its
-  // start. A split is taken only when it shortens the modelled makespan by
-  // 5 % or more. (Measured, 8192 × 1024 × 8192 on one B200: 4 pieces per
-  // item gave 135.7 µs against 129.2 µs whole; 8192 × 2048 × 8192: 2 pieces
-  // for the last 108 items gave 242.4 µs against 247.7 µs.)
-  constexpr int64_t kPieceCost = 8;
+                          int64_t* tail_items, int64_t* tail_segs) {
+  // Cost model in ring fills per slot (every item has `fills` fills). The
+  // whole waves before the last full one keep their items whole; the rest
+  // (one full wave plus the partial one, L items) is cut into `slots` equal
+  // runs of consecutive fills — a run starts and ends inside items, so a
+  // slot works on up to three segments, the partial ones reduce-added into
+  // C. Each segment beyond a slot's first is charged kSegCost fills (its
+  // start and its partial-tile reduce-add). The tail is taken only when it
+  // shortens the modelled makespan by 5 % or more. (Measured on one B200:
+  // cutting every item of the 8-way slice of 8192³ into 4 K pieces instead
+  // lost 5 %; the stream-K run bounds the partial segments to two per slot.)
+  constexpr int64_t kSegCost = 8;
   *dp_items = items;
   *tail_items = 0;
-  *tail_parts = 1;
+  *tail_segs = 0;
   if (slots <= 1 || items <= 0 || items % slots == 0 || fills < 16) return;
   const int64_t whole = (items + slots - 1) / slots * fills;
-  int64_t best = whole - whole * 5 / 100;
   const int64_t d = std::max<int64_t>(0, items / slots - 1) * slots;
   const int64_t L = items - d;
-  for (int64_t s = 2; s <= 8 && fills / s >= 8; ++s) {
-    const int64_t pieces = L * s;
-    if (d + pieces > std::numeric_limits<int32_t>::max()) break;
-    const int64_t t = d / slots * fills + (pieces + slots - 1) / slots * ((fills + s - 1) / s + kPieceCost);
-    if (t < best) {
-      best = t;
-      *dp_items = d;
-      *tail_items = L;
-      *tail_parts = s;
-    }
+  const int64_t U = L * fills;
+  int64_t segs = 1;
+  for (int64_t p = 0; p < slots; ++p) {
+    const int64_t u0 = p * U / slots, u1 = (p + 1) * U / slots;
+    if (u1 > u0) segs = std::max<int64_t>(segs, (u1 - 1) / fills - u0 / fills + 1);
+  }
+  const int64_t t = d / slots * fills + (U + slots - 1) / slots + kSegCost * (segs - 1);
+  if (t < whole - whole * 5 / 100 && d + segs * slots <= std::numeric_limits<int32_t>::max()) {
+    *dp_items = d;
+    *tail_items = L;
+    *tail_segs = segs;
   }
 }
 
@@ -463,13 +465,19 @@ tbStatus tb_plan_build(const tb_matmul_desc& d, int device, int num_sms, tb_matm
   // last items are cut into K pieces that fill the idle slots.
   p.dp_items = p.work_items;
   p.tail_items = 0;
-  p.tail_parts = 1;
+  p.tail_segs = 0;
+  p.tail_slots = 0;
+  p.tail_fills = 0;
   const bool exact_hw = d.block_m * (p.fuse == 1 || p.fuse == 4 ? 2 : 1) == (int64_t)p.cta_m * p.sub_m &&
                         d.block_n * (p.fuse >= 2 ? 2 : 1) == (int64_t)p.cta_n * p.sub_n;
   if (!d.deterministic && split_k == 1 && d.c_dtype == TB_F32 && d.beta && !exprs && exact_hw)
     tb_choose_tail_split(p.work_items, resident, ceil_div(d.k, p.kb), &p.dp_items, &p.tail_items,
-                         &p.tail_parts);
-  p.positions = p.dp_items + p.tail_items * p.tail_parts;
+                         &p.tail_segs);
+  if (p.tail_items) {
+    p.tail_slots = resident;
+    p.tail_fills = ceil_div(d.k, p.kb);
+  }
+  p.positions = p.dp_items + p.tail_segs * p.tail_slots;
   p.grid = p.ctas_per_tile * std::max<int64_t>(1, std::min<int64_t>(p.positions, resident));
   // Small problems (every item's K range within 128 elements on a one-CTA
   // tile at most 128 wide) are launch- and latency-bound: they run on the
@@ -573,8 +581,9 @@ extern "C" tbStatus tb_matmul_plan_describe(const tb_matmul_plan* plan, char* bu
   o << "\"program_subtiles\": [" << plan->sub_m << ", " << plan->sub_n << "], ";
   o << "\"tail_split\": ";
   if (plan->tail_items)
-    o << "{\"whole_items\": " << plan->dp_items << ", \"split_items\": " << plan->tail_items
-      << ", \"k_pieces\": " << plan->tail_parts << "}, ";
+    o << "{\"whole_items\": " << plan->dp_items << ", \"stream_k_items\": " << plan->tail_items
+      << ", \"slots\": " << plan->tail_slots << ", \"segments_per_slot\": " << plan->tail_segs
+      << ", \"fills_per_item\": " << plan->tail_fills << "}, ";
   else
     o << "null, ";
   o << "\"walk_positions\": " << plan->positions << ", ";

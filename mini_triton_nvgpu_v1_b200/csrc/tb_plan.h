@@ -65,10 +65,13 @@ struct tb_matmul_plan {
   int32_t fuse;
   int64_t work_items;          // total_programs / programs per item (1, 2 or 4), or × sub-tiles
   int32_t sub_m, sub_n;        // hardware tiles per program along M / N (programs larger than a tile)
-  // Tail balancing (tb_choose_tail_split): walk positions [0, dp_items) run
-  // whole work items, the last tail_items items run as tail_parts K pieces
-  // each (reduce-added into C); positions = dp_items + tail_items·tail_parts.
-  int64_t dp_items, tail_items, tail_parts, positions;
+  // Tail balancing (tb_choose_tail_split, a stream-K tail): walk positions
+  // [0, dp_items) run whole work items; the last tail_items items form one
+  // run of tail_items · tail_fills ring fills split evenly over tail_slots
+  // slots, each slot taking up to tail_segs segments (parts of one item; a
+  // partial one is reduce-added into C). positions = dp_items +
+  // tail_segs · tail_slots.
+  int64_t dp_items, tail_items, tail_slots, tail_segs, tail_fills, positions;
   // Latency kernel (tb_gemm_small_kernel): one-CTA tiles at most 128 wide,
   // every work item at most 128 K elements, row-major operands, at most
   // four items per CTA.
@@ -105,10 +108,10 @@ tbStatus tb_plan_build(const tb_matmul_desc& d, int device, int num_sms, tb_matm
 // JSON facts of a dynamic plan; tb_dynamic.cpp.
 std::string tb_describe_dynamic(const tb_matmul_plan* plan);
 
-// Chooses the tail split for `items` equal work items of `fills` ring fills
-// on `slots` resident slots (tb_plan.cpp).
+// Chooses the stream-K tail for `items` equal work items of `fills` ring
+// fills on `slots` resident slots (tb_plan.cpp); *tail_items = 0: none.
 void tb_choose_tail_split(int64_t items, int64_t slots, int64_t fills, int64_t* dp_items,
-                          int64_t* tail_items, int64_t* tail_parts);
+                          int64_t* tail_items, int64_t* tail_segs);
 
 // Thread-local error message helpers (tb_plan.cpp).
 tbStatus tb_fail(tbStatus code, const std::string& msg);

@@ -99,3 +99,50 @@ def test_two_rank_fused_kshard(cuda, shape, knobs):
     for rank, err, err2, tol in res:
         assert err <= 2 * tol, (rank, err)
         assert err2 <= tol, (rank, err2)
+
+
+def _nshard_worker(rank, world, q, m, n, k, knobs):
+    import torch
+    torch.cuda.set_device(rank)
+    import mini_triton_nvgpu_v1_b200 as tb
+    from mini_triton_nvgpu_v1_b200 import parallel as par
+    import oracle
+    dev = torch.device("cuda", rank)
+    rng = np.random.default_rng(43)
+    A = rng.uniform(-1, 1, (m, k)).astype(np.float16)
+    B = rng.uniform(-1, 1, (k, n)).astype(np.float16)
+    Cin = rng.standard_normal((m, n)).astype(np.float32)
+    sh = par.NShard(tb.KernelConfig(m=m, n=n, k=k, **knobs), rank, world, rank)
+    c0, nc = sh.col0, sh.ncols
+    tA = torch.from_numpy(A).to(dev)
+    tB = torch.from_numpy(B[:, c0:c0 + nc].copy()).to(dev)
+    tC = torch.from_numpy(Cin[:, c0:c0 + nc].copy()).to(dev)
+    sh.run(tA, tB, tC)
+    torch.cuda.synchronize()
+    want = oracle.matmul_ref(A, B, Cin)[:, c0:c0 + nc]
+    q.put((rank, c0, nc, float(np.abs(tC.cpu().numpy() - want).max()), oracle.tolerance(k)))
+
+
+@pytest.mark.parametrize("shape,knobs", [
+    ((1024, 2304, 1024), dict(block_m=256, block_n=256, block_k=64)),
+    ((520, 1000, 700), dict(block_m=128, block_n=128, block_k=64, exact_tile=False)),
+])
+def test_two_rank_nshard(cuda, shape, knobs):
+    """tb_matmul_run_nshard on two GPUs, one process each, no collective: the
+    two column slices cover C once and each matches the oracle."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_nshard_worker, args=(r, 2, q, *shape, knobs)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[0][1] == 0 and res[0][2] + res[1][2] == shape[1] and res[1][1] == res[0][2]
+    for rank, c0, nc, err, tol in res:
+        assert err <= tol, (rank, err)

@@ -107,19 +107,49 @@ def test_large_program_tiles_run_as_subtiles(bm, bn, tile, sub):
 
 
 def test_tail_split_plan_facts():
-    """8192 x 2048 x 8192 (one rank of a 4-way N-shard): 256 pair items on
-    74 CTA pairs; two whole waves, then the last 108 items in two K pieces.
-    f16 C, beta = 0, split-K and deterministic plans keep whole items, and
-    so does the 8-way slice (128 items), where pieces measured slower."""
-    p = plan(8192, 2048, 8192, 256, 256, 64)
-    ts = p.info["tail_split"]
-    assert ts == {"whole_items": 148, "split_items": 108, "k_pieces": 2}
-    assert p.info["walk_positions"] == 148 + 108 * 2 and p.info["grid"] == 148
+    """8192 x 1024 x 8192 (one rank of an 8-way N-shard): 128 pair items on
+    74 CTA pairs; the whole run of 128 · 128 ring fills is cut into 74 equal
+    ranges (stream-K tail), at most three segments per slot. The 4-way slice
+    keeps two whole waves and spreads the last 108 items. f16 C, beta = 0,
+    split-K and deterministic plans keep whole items; 8192^3 (13.8 waves)
+    gains too little."""
+    p = plan(8192, 1024, 8192, 256, 256, 64)
+    assert p.info["tail_split"] == {"whole_items": 0, "stream_k_items": 128, "slots": 74,
+                                    "segments_per_slot": 3, "fills_per_item": 128}
+    assert p.info["walk_positions"] == 3 * 74 and p.info["grid"] == 148
+    q = plan(8192, 2048, 8192, 256, 256, 64)
+    assert q.info["tail_split"]["whole_items"] == 148 and q.info["tail_split"]["stream_k_items"] == 108
     for kw in (dict(c_dtype="f16"), dict(beta=0), dict(deterministic=True), dict(split_k=2)):
-        q = plan(8192, 2048, 8192, 256, 256, 64, **kw)
-        assert q.info["tail_split"] is None, kw
-    assert plan(8192, 1024, 8192, 256, 256, 64).info["tail_split"] is None
+        r = plan(8192, 1024, 8192, 256, 256, 64, **kw)
+        assert r.info["tail_split"] is None, kw
     assert plan(8192, 8192, 8192, 256, 256, 64).info["tail_split"] is None
+
+
+def _stream_k_cover(items, fills, slots, segs):
+    """Restates the kernel's position → (item, fill range) rule and checks
+    that the segments cover every fill of the tail exactly once."""
+    U = items * fills
+    seen = [[0] * fills for _ in range(items)]
+    for seg in range(segs):
+        for q in range(slots):
+            u0, u1 = q * U // slots, (q + 1) * U // slots
+            i = u0 // fills + seg
+            if i >= items:
+                continue
+            b = i * fills
+            f0, f1 = max(u0, b) - b, min(u1, b + fills) - b
+            for f in range(f0, max(f0, f1)):
+                seen[i][f] += 1
+    return all(c == 1 for row in seen for c in row)
+
+
+@pytest.mark.parametrize("n", [1024, 2048, 2560, 3072])
+def test_stream_k_tail_covers_every_fill_once(n):
+    p = plan(8192, n, 8192, 256, 256, 64)
+    ts = p.info["tail_split"]
+    if ts is None:
+        pytest.skip("no tail for this shape")
+    assert _stream_k_cover(ts["stream_k_items"], ts["fills_per_item"], ts["slots"], ts["segments_per_slot"])
 
 
 # ---------------------------------------------------------------- mapping

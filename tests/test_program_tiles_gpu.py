@@ -1,7 +1,7 @@
 """GPU parity for the work decompositions that do not change a program's
 result: program tiles larger than every hardware tile (run as sub-tiles),
-the tail split (the last work items cut into K pieces that are reduce-added
-into C), and the N-shard entry point run rank by rank on one GPU. Every
+the stream-K tail (the last work items' K fills spread evenly over the
+slots, partial items reduce-added into C), and the N-shard entry point run rank by rank on one GPU. Every
 element is compared with the CPU oracle, tolerance 1e-2·sqrt(K/32)."""
 from __future__ import annotations
 
@@ -69,9 +69,10 @@ def test_large_program_tiles(cuda, shape, knobs, sub, out):
                          ids=["pair", "pair_ragged_m", "fused_128", "fused_256x128"])
 @pytest.mark.parametrize("persistent", [False, True])
 def test_tail_split_matches_oracle_and_whole_items(cuda, shape, tile, persistent):
-    """Plans whose last wave is partly idle cut the tail items into K
-    pieces; the result matches the oracle and the deterministic (whole
-    item) run within tolerance, and the deterministic run repeats bitwise."""
+    """Plans whose last wave is partly idle spread the tail items' K fills
+    evenly over the slots (stream-K; partial items reduce-added into C); the
+    result matches the oracle and the deterministic (whole item) run within
+    tolerance, and the deterministic run repeats bitwise."""
     import torch
     import mini_triton_nvgpu_v1_b200 as tb
     import oracle
