@@ -60,6 +60,9 @@ def parse():
                     help="gemm8192: the headline 8192^3 N-sharded GEMM; splitk: the skinny "
                          "512x512x65536 split-K config (K-sharded + reduce-scatter at N>1)")
     ap.add_argument("--only", default=None, help="sweep: only the configs whose name contains this")
+    ap.add_argument("--launches", type=int, default=0,
+                    help="sweep: run each selected config this many times and time nothing "
+                         "(a fixed launch sequence for a profiler)")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
                     help="gemm8192 at N>1: strong = the fixed 8192^3 problem split along N "
                          "(BASELINE's config); weak = 8192 columns per GPU")
@@ -663,6 +666,15 @@ def run_sweep(args):
         C = torch.zeros(m, n, device=dev, dtype=torch.float16 if cdt == "f16" else torch.float32)
         ws = None
         f = lambda: tb.matmul(A, B, C, workspace=ws, **kn)
+        if getattr(args, "launches", 0):
+            for _ in range(args.launches):
+                f()
+            torch.cuda.synchronize()
+            tb.device_status()
+            print(json.dumps({"workload": "sweep", "config": name, "launches": args.launches}), flush=True)
+            del A, B, C
+            torch.cuda.empty_cache()
+            continue
         for _ in range(5):
             f()
         torch.cuda.synchronize()
