@@ -207,8 +207,9 @@ __host__ __device__ __forceinline__ int32_t imin(int32_t a, int32_t b) { return 
 template <int HM, int HN>
 __host__ __device__ __forceinline__ Extent program_extent(const KParams& p, int32_t pos, int32_t kb) {
   int32_t w = pos;
-  int32_t f0 = 0, f1 = -1;  // the position's fills of its item (stream-K tail), or all
-  if (pos >= p.dp_items) {
+  int32_t f0 = 0, f1 = 0;   // the position's fills of its item (stream-K tail)
+  const bool tail = pos >= p.dp_items;
+  if (tail) {
     const int32_t t = pos - p.dp_items;
     const int32_t seg = t / p.tail_slots, q = t % p.tail_slots;
     const int64_t U = (int64_t)p.tail_items * p.tail_fills;
@@ -241,8 +242,8 @@ __host__ __device__ __forceinline__ Extent program_extent(const KParams& p, int3
   e.nkb = e.k_end > e.k_begin && e.rows > 0 && e.cols > 0 ? (e.k_end - e.k_begin + kb - 1) / kb : 0;
   e.part = wk.part;
   e.piece = false;
-  if (f1 >= 0) {
-    if (f1 <= f0) {  // empty: no loads, no MMA, no stores
+  if (tail) {
+    if (f1 <= f0) {  // empty (its range ends before this item): no loads, no MMA, no stores
       e.nkb = 0;
       e.cols = 0;
       return e;

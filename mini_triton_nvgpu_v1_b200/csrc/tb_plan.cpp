@@ -97,8 +97,12 @@ void tb_choose_tail_split(int64_t items, int64_t slots, int64_t fills, int64_t* 
     const int64_t u0 = p * U / slots, u1 = (p + 1) * U / slots;
     if (u1 > u0) segs = std::max<int64_t>(segs, (u1 - 1) / fills - u0 / fills + 1);
   }
-  const int64_t t = d / slots * fills + (U + slots - 1) / slots + kSegCost * (segs - 1);
-  if (t < whole - whole * 5 / 100 && d + segs * slots <= std::numeric_limits<int32_t>::max()) {
+  // Runs shorter than kMinRun fills are all start-up and reduce-add: keep
+  // such problems whole (e.g. 1024³ on 74 pairs would give 3–4 fills a slot).
+  constexpr int64_t kMinRun = 32;
+  const int64_t run = (U + slots - 1) / slots;
+  const int64_t t = d / slots * fills + run + kSegCost * (segs - 1);
+  if (run >= kMinRun && t < whole - whole * 5 / 100 && d + segs * slots <= std::numeric_limits<int32_t>::max()) {
     *dp_items = d;
     *tail_items = L;
     *tail_segs = segs;
