@@ -111,7 +111,7 @@ FULL = [
     dict(shape=(8192, 8192, 8192), knobs=dict(block_m=256, block_n=256, block_k=64, persistent=True,
                                               num_ctas=148), dist="uniform", seed=9, out="f16"),
     # one rank's slice of the 8-way N-sharded 8192^3 problem: 128 pair work
-    # items on 74 CTA pairs, run as a stream-K tail
+    # items on 74 CTA pairs (whole items: no whole wave before a tail)
     dict(shape=(8192, 1024, 8192), knobs=dict(block_m=256, block_n=256, block_k=64, group_m=8),
          dist="normal", seed=10, out="f32"),
     # a 4-way slice: two whole waves, then 108 items spread stream-K
@@ -122,7 +122,7 @@ FULL = [
 
 @pytest.mark.parametrize("cfg", FULL, ids=["grouped_8192", "ragged_scaleup_4096_f16", "splitk_serial_skinny",
                                           "splitk_serial_skinny_pair", "splitk_parallel_skinny_pair",
-                                          "persistent_2048_f16", "persistent_8192_f16", "nshard8_slice_tail",
+                                          "persistent_2048_f16", "persistent_8192_f16", "nshard8_slice",
                                           "nshard4_slice_tail"])
 def test_fullsize_every_element(cuda, cfg):
     """Every element of each full-size BASELINE config against the CPU

@@ -107,18 +107,18 @@ def test_large_program_tiles_run_as_subtiles(bm, bn, tile, sub):
 
 
 def test_tail_split_plan_facts():
-    """8192 x 1024 x 8192 (one rank of an 8-way N-shard): 128 pair items on
-    74 CTA pairs; the whole run of 128 · 128 ring fills is cut into 74 equal
-    ranges (stream-K tail), at most three segments per slot. The 4-way slice
-    keeps two whole waves and spreads the last 108 items. f16 C, beta = 0,
+    """8192 x 2048 x 8192 (one rank of a 4-way N-shard): 256 pair items on
+    74 CTA pairs; two whole waves, then the last 108 items' 108 · 128 ring
+    fills cut into 74 equal ranges (stream-K tail), at most three segments
+    per slot. The 8-way slice (no whole wave first) stays whole. f16 C, beta = 0,
     split-K and deterministic plans keep whole items; 8192^3 (13.8 waves)
     gains too little."""
-    p = plan(8192, 1024, 8192, 256, 256, 64)
-    assert p.info["tail_split"] == {"whole_items": 0, "stream_k_items": 128, "slots": 74,
+    p = plan(8192, 2048, 8192, 256, 256, 64)
+    assert p.info["tail_split"] == {"whole_items": 148, "stream_k_items": 108, "slots": 74,
                                     "segments_per_slot": 3, "fills_per_item": 128}
-    assert p.info["walk_positions"] == 3 * 74 and p.info["grid"] == 148
-    q = plan(8192, 2048, 8192, 256, 256, 64)
-    assert q.info["tail_split"]["whole_items"] == 148 and q.info["tail_split"]["stream_k_items"] == 108
+    assert p.info["walk_positions"] == 148 + 3 * 74 and p.info["grid"] == 148
+    # no whole wave before the tail: measured slower, kept whole
+    assert plan(8192, 1024, 8192, 256, 256, 64).info["tail_split"] is None
     for kw in (dict(c_dtype="f16"), dict(beta=0), dict(deterministic=True), dict(split_k=2)):
         r = plan(8192, 1024, 8192, 256, 256, 64, **kw)
         assert r.info["tail_split"] is None, kw
