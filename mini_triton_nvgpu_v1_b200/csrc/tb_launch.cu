@@ -984,8 +984,8 @@ struct SmallCfg {
 template <int BN, typename OutT>
 __global__ void __launch_bounds__(128, 1)
     tb_gemm_small_kernel(const __grid_constant__ KParams pk, const __grid_constant__ SmallTab tab,
-                         const uint16_t* __restrict__ A, int64_t lda, const uint16_t* __restrict__ B,
-                         int64_t ldb) {
+                         const __grid_constant__ CUtensorMap tmC, const uint16_t* __restrict__ A,
+                         int64_t lda, const uint16_t* __restrict__ B, int64_t ldb) {
   using Sc = SmallCfg<BN, OutT>;
   // The parameters come through the constant bank, which each launch
   // refills: reading them field by field inside the dependent mapping
@@ -1005,13 +1005,21 @@ __global__ void __launch_bounds__(128, 1)
   uint8_t* sB = smem + kSmallABytes;
   uint8_t* sCin = sB + Sc::kBBytes;
   uint64_t* done = reinterpret_cast<uint64_t*>(sCin + 128 * Sc::kCinStride);
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* cin_bar = done + 1;  // C_in boxes loaded by TMA (p.tma_out == kTmaStoreC)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 2);
+  // C_in by TMA: [32 rows × 128 bytes] boxes, 128-byte swizzled, box (w, j)
+  // (row group w, 128-byte column chunk j) at sCin + (w · kCinChunks + j) · 4 KB
+  constexpr int kCinChunks = BN * (int)sizeof(OutT) / 128;
+  constexpr int kCinCols = 128 / (int)sizeof(OutT);  // columns per chunk
   const int t = threadIdx.x;
   const int warp = t / 32;
   if (t == 0) {
     mbar_init(smem_addr(done), 1);
+    mbar_init(smem_addr(cin_bar), 1);
     fence_mbar_init();
   }
+  uint32_t cin_phase = 0;
+  const bool cin_tma = p.tma_out == kTmaStoreC && p.beta && p.epilogue == kEpiStore;
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const uint32_t idesc = idesc_f16_f32(128, BN, 0, 1);
   uint32_t phase = 0;
@@ -1033,6 +1041,16 @@ __global__ void __launch_bounds__(128, 1)
       kvalid = e.nkb > 0 ? e.k_end - e.k_begin : 0;  // <= kSmallK (plan rule)
     }
     const int k16 = (kvalid + 15) / 16 * 16;                 // K covered by the MMA steps
+    // ---- C_in by TMA (one thread, a handful of boxes; the rest of the tile's
+    //      rows and columns come back as zero past M/N)
+    if (cin_tma && t == 0) {
+      const int nrg = min(4, (e.rows + 31) / 32), nch = (e.cols + kCinCols - 1) / kCinCols;
+      mbar_expect_tx(smem_addr(cin_bar), (uint32_t)(nrg * nch * 4096));
+      for (int w = 0; w < nrg; ++w)
+        for (int j = 0; j < nch; ++j)
+          tma_load_2d(smem_addr(sCin + (size_t)(w * kCinChunks + j) * 4096), &tmC, smem_addr(cin_bar),
+                      e.n0 + j * kCinCols, e.m0 + 32 * w);
+    }
     // ---- stage A (K-major, two [128 × 64] sub-tiles; thread t copies row t)
     //      and B (MN-major [kSmallK × 64] boxes; thread t < k16 copies K row
     //      t), 16-byte chunks, zero past K / M / N
@@ -1076,6 +1094,16 @@ __global__ void __launch_bounds__(128, 1)
     }
     cp_async_wait_all();
     fence_proxy_async_smem();  // cp.async wrote through the generic proxy; the MMA reads via async
+    if (cin_tma) {
+      const long long t0 = clock64();
+      while (!mbar_try_wait(smem_addr(cin_bar), cin_phase)) {
+        if (clock64() - t0 > kWaitBudgetCycles) {
+          record_error(TB_ERR_DEVICE_TIMEOUT, kSiteEpilogue);
+          break;
+        }
+      }
+      cin_phase ^= 1u;
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -1121,7 +1149,35 @@ __global__ void __launch_bounds__(128, 1)
       if (p.epilogue == kEpiStore) {
         OutT* dst = reinterpret_cast<OutT*>(p.C) + grow * p.ldc + gcol;
         if (p.beta) {
-          if (cin_smem) {
+          if (cin_tma) {
+            // row t of box (warp, chunk): 16-byte piece u at piece u ^ (t % 8)
+            const int lane = t % 32;
+            const int byte0 = c0 * (int)sizeof(OutT);
+            const uint8_t* crow = sCin + (size_t)(warp * kCinChunks + byte0 / 128) * 4096 + lane * 128;
+            const int u0 = (byte0 % 128) / 16;
+            float c[32];
+            if constexpr (sizeof(OutT) == 4) {
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const float4 q4 = *reinterpret_cast<const float4*>(crow + ((u ^ (lane & 7)) * 16));
+                c[4 * u] = q4.x; c[4 * u + 1] = q4.y; c[4 * u + 2] = q4.z; c[4 * u + 3] = q4.w;
+              }
+            } else {
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const uint4 q4 = *reinterpret_cast<const uint4*>(crow + (((u0 + u) ^ (lane & 7)) * 16));
+                const uint32_t w4[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[w]));
+                  c[8 * u + 2 * w] = f.x; c[8 * u + 2 * w + 1] = f.y;
+                }
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < ncol) v[i] += c[i];
+          } else if (cin_smem) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               float c = 0.f;
@@ -1385,7 +1441,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 std::atomic<bool> g_small_attr_set[2][2][kMaxDevices];
 
 template <int BN, typename OutT>
-tbStatus launch_small_bn(const tb_matmul_plan* plan, const KParams& kp, const void* A, int64_t lda,
+tbStatus launch_small_bn(const tb_matmul_plan* plan, const KParams& kp, const CUtensorMap& tcm,
+                         const void* A, int64_t lda,
                          const void* B, int64_t ldb, cudaStream_t stream, int ot) {
   auto kern = tb_gemm_small_kernel<BN, OutT>;
   constexpr size_t smem = SmallCfg<BN, OutT>::kSmem;
@@ -1411,7 +1468,7 @@ tbStatus launch_small_bn(const tb_matmul_plan* plan, const KParams& kp, const vo
     tab.kvalid[pos] = (int16_t)(e.nkb > 0 ? e.k_end - e.k_begin : 0);
     tab.part[pos] = (int16_t)e.part;
   }
-  kern<<<(unsigned)plan->grid, 128, smem, stream>>>(kp, tab, static_cast<const uint16_t*>(A), lda,
+  kern<<<(unsigned)plan->grid, 128, smem, stream>>>(kp, tab, tcm, static_cast<const uint16_t*>(A), lda,
                                                     static_cast<const uint16_t*>(B), ldb);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
@@ -1420,10 +1477,10 @@ tbStatus launch_small_bn(const tb_matmul_plan* plan, const KParams& kp, const vo
 }
 
 template <typename OutT>
-tbStatus launch_small(const tb_matmul_plan* plan, const KParams& kp, const void* A, int64_t lda,
-                      const void* B, int64_t ldb, cudaStream_t stream, int ot) {
-  return plan->cta_n == 64 ? launch_small_bn<64, OutT>(plan, kp, A, lda, B, ldb, stream, ot)
-                           : launch_small_bn<128, OutT>(plan, kp, A, lda, B, ldb, stream, ot);
+tbStatus launch_small(const tb_matmul_plan* plan, const KParams& kp, const CUtensorMap& tcm, const void* A,
+                      int64_t lda, const void* B, int64_t ldb, cudaStream_t stream, int ot) {
+  return plan->cta_n == 64 ? launch_small_bn<64, OutT>(plan, kp, tcm, A, lda, B, ldb, stream, ot)
+                           : launch_small_bn<128, OutT>(plan, kp, tcm, A, lda, B, ldb, stream, ot);
 }
 
 tbStatus pack_rows_f16(const void* src, int64_t ld_src, void* dst, int64_t ld_dst, int64_t rows,
@@ -1617,7 +1674,15 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   CUtensorMap tcm;
   memset(&tcm, 0, sizeof(tcm));
   kp.tma_out = kTmaNone;
-  if (plan->small) kp.cin_smem = kp.vec_c;  // every item stages its C_in rows (direct epilogue)
+  if (plan->small) {
+    // every item stages its C_in tile: by TMA boxes when C is TMA-addressable
+    // (the kernel reads kp.tma_out == kTmaStoreC as "C map valid"), else by
+    // per-row cp.async
+    const bool cmap = d.beta && plan->epilogue == kEpiStore && aligned16(Cp) &&
+                      ldc % (d.c_dtype == TB_F16 ? 8 : 4) == 0;
+    kp.cin_smem = cmap ? 0 : kp.vec_c;
+    if (cmap) kp.tma_out = kTmaStoreC;
+  }
   const bool exact_hw_tile = !plan->small &&
       d.block_m * (plan->fuse == 1 || plan->fuse == 4 ? 2 : 1) == (int64_t)plan->cta_m * plan->sub_m &&
       d.block_n * (plan->fuse >= 2 ? 2 : 1) == (int64_t)plan->cta_n * plan->sub_n;
@@ -1663,8 +1728,8 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   }
 
   if (plan->small)
-    st = d.c_dtype == TB_F16 ? launch_small<__half>(plan, kp, A, lda, B, ldb, stream, 1)
-                             : launch_small<float>(plan, kp, A, lda, B, ldb, stream, 0);
+    st = d.c_dtype == TB_F16 ? launch_small<__half>(plan, kp, tcm, A, lda, B, ldb, stream, 1)
+                             : launch_small<float>(plan, kp, tcm, A, lda, B, ldb, stream, 0);
   else
     st = d.c_dtype == TB_F16 ? dispatch_tile<__half>(plan, ta, tbm, tcm, kp, stream, 1)
                              : dispatch_tile<float>(plan, ta, tbm, tcm, kp, stream, 0);
