@@ -952,14 +952,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------- small
 // Latency kernel for problems whose every work item has at most kSmallK K
 // elements on a one-CTA 128 × BN tile (the BASELINE's 64×64×32, 96×80×32,
-// 192×128×32 and split 64×64×64 programs). No tensor maps, no warp roles, no
-// pipeline: all 128 threads copy the item's A rows, B rows and C_in row into
-// shared memory at once with cp.async — A and B straight into the
-// 128-byte-swizzled layout the UMMA descriptors read (16-byte chunk j of row r
-// at chunk j ^ (r % 8)), zero-filled past the item's K range and past M/N —
-// then one thread issues the K/16 tcgen05.mma steps, and every thread takes
-// its accumulator row from TMEM and stores it. A CTA walks several items in
-// turn when there are more items than CTAs (persistent plans).
+// 192×128×32 and split 64×64×64 programs). No warp roles and no pipeline:
+// one thread brings the item's A and B boxes (and the C_in tile, when C is
+// TMA-addressable) in with TMA on one mbarrier while warp 0 allocates TMEM,
+// then issues the K/16 tcgen05.mma steps, and every thread takes its
+// accumulator row from TMEM and stores it. A CTA walks several items in turn
+// when there are more items than CTAs (persistent plans).
 constexpr int kSmallK = 128;
 // Work of the first kSmallTab walk positions, derived on the host (the same
 // program_extent): a single thread's chain of mapping arithmetic and
@@ -984,8 +982,8 @@ struct SmallCfg {
 template <int BN, typename OutT>
 __global__ void __launch_bounds__(128, 1)
     tb_gemm_small_kernel(const __grid_constant__ KParams pk, const __grid_constant__ SmallTab tab,
-                         const __grid_constant__ CUtensorMap tmC, const uint16_t* __restrict__ A,
-                         int64_t lda, const uint16_t* __restrict__ B, int64_t ldb) {
+                         const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmC) {
   using Sc = SmallCfg<BN, OutT>;
   // The parameters come through the constant bank, which each launch
   // refills: reading them field by field inside the dependent mapping
@@ -1005,7 +1003,7 @@ __global__ void __launch_bounds__(128, 1)
   uint8_t* sB = smem + kSmallABytes;
   uint8_t* sCin = sB + Sc::kBBytes;
   uint64_t* done = reinterpret_cast<uint64_t*>(sCin + 128 * Sc::kCinStride);
-  uint64_t* cin_bar = done + 1;  // C_in boxes loaded by TMA (p.tma_out == kTmaStoreC)
+  uint64_t* ld_bar = done + 1;  // the item's TMA loads (A, B and, when C is TMA-addressable, C_in)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 2);
   // C_in by TMA: [32 rows × 128 bytes] boxes, 128-byte swizzled, box (w, j)
   // (row group w, 128-byte column chunk j) at sCin + (w · kCinChunks + j) · 4 KB
@@ -1015,10 +1013,13 @@ __global__ void __launch_bounds__(128, 1)
   const int warp = t / 32;
   if (t == 0) {
     mbar_init(smem_addr(done), 1);
-    mbar_init(smem_addr(cin_bar), 1);
+    mbar_init(smem_addr(ld_bar), 1);
     fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
   }
-  uint32_t cin_phase = 0;
+  __syncthreads();
+  uint32_t ld_phase = 0;
   const bool cin_tma = p.tma_out == kTmaStoreC && p.beta && p.epilogue == kEpiStore;
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const uint32_t idesc = idesc_f16_f32(128, BN, 0, 1);
@@ -1041,40 +1042,30 @@ __global__ void __launch_bounds__(128, 1)
       kvalid = e.nkb > 0 ? e.k_end - e.k_begin : 0;  // <= kSmallK (plan rule)
     }
     const int k16 = (kvalid + 15) / 16 * 16;                 // K covered by the MMA steps
-    // ---- C_in by TMA (one thread, a handful of boxes; the rest of the tile's
-    //      rows and columns come back as zero past M/N)
-    if (cin_tma && t == 0) {
-      const int nrg = min(4, (e.rows + 31) / 32), nch = (e.cols + kCinCols - 1) / kCinCols;
-      mbar_expect_tx(smem_addr(cin_bar), (uint32_t)(nrg * nch * 4096));
+    // ---- one thread brings the item in with TMA on one mbarrier: A as
+    //      [128 m × 64 k] K-major boxes, B as [128 k × 64 n] MN-major boxes
+    //      (both 128-byte swizzled, the layouts the UMMA descriptors read;
+    //      zero past M/N/K), and, when C is TMA-addressable, the C_in tile as
+    //      [32 rows × 128 bytes] boxes. Only the K steps below the item's
+    //      range are issued: its end is a multiple of 16 (block_k) or the end
+    //      of K, where the boxes read zeros.
+    if (t == 0) {
+      const int na = (k16 + 63) / 64;
+      const int nrg = cin_tma ? min(4, (e.rows + 31) / 32) : 0;
+      const int nch = cin_tma ? (e.cols + kCinCols - 1) / kCinCols : 0;
+      const uint32_t bytes =
+          k16 > 0 ? (uint32_t)(na * kSmallASub + (BN / 64) * kSmallBox + nrg * nch * 4096) : (uint32_t)(nrg * nch * 4096);
+      mbar_expect_tx(smem_addr(ld_bar), bytes);
+      if (k16 > 0) {
+        for (int j = 0; j < na; ++j)
+          tma_load_2d(smem_addr(sA + (size_t)j * kSmallASub), &tmA, smem_addr(ld_bar), e.k_begin + 64 * j, e.m0);
+        for (int j = 0; j < BN / 64; ++j)
+          tma_load_2d(smem_addr(sB + (size_t)j * kSmallBox), &tmB, smem_addr(ld_bar), e.n0 + 64 * j, e.k_begin);
+      }
       for (int w = 0; w < nrg; ++w)
         for (int j = 0; j < nch; ++j)
-          tma_load_2d(smem_addr(sCin + (size_t)(w * kCinChunks + j) * 4096), &tmC, smem_addr(cin_bar),
+          tma_load_2d(smem_addr(sCin + (size_t)(w * kCinChunks + j) * 4096), &tmC, smem_addr(ld_bar),
                       e.n0 + j * kCinCols, e.m0 + 32 * w);
-    }
-    // ---- stage A (K-major, two [128 × 64] sub-tiles; thread t copies row t)
-    //      and B (MN-major [kSmallK × 64] boxes; thread t < k16 copies K row
-    //      t), 16-byte chunks, zero past K / M / N
-    {
-      const int64_t gm = (int64_t)e.m0 + t;
-      const uint16_t* arow = A + gm * lda + e.k_begin;
-      uint8_t* drow = sA + t * 128;
-      for (int k = 0; k < k16; k += 8) {
-        const uint32_t bytes = gm < p.M && k < kvalid ? (uint32_t)min(16, (kvalid - k) * 2) : 0u;
-        cp_async_16(smem_addr(drow + (k / 64) * kSmallASub + (((k / 8) % 8) ^ (t % 8)) * 16),
-                    bytes ? arow + k : A, bytes);
-      }
-    }
-    if (t < k16) {
-      const uint16_t* brow = B + (int64_t)(e.k_begin + t) * ldb + e.n0;
-      uint8_t* drow = sB + t * 128;
-#pragma unroll
-      for (int nc = 0; nc < BN / 8; ++nc) {
-        const int64_t gn = (int64_t)e.n0 + nc * 8;
-        const uint32_t bytes =
-            t < kvalid && gn < p.N ? (uint32_t)(p.N - gn >= 8 ? 16 : (p.N - gn) * 2) : 0u;
-        cp_async_16(smem_addr(drow + (nc / 8) * kSmallBox + ((nc % 8) ^ (t % 8)) * 16),
-                    bytes ? brow + nc * 8 : B, bytes);
-      }
     }
     // ---- this thread's C_in row, fetched alongside the operands
     const bool row_ok = t < e.rows;
@@ -1092,18 +1083,18 @@ __global__ void __launch_bounds__(128, 1)
       tmem_alloc(smem_addr(tmem_holder), BN);
       tmem_relinquish();
     }
-    cp_async_wait_all();
-    fence_proxy_async_smem();  // cp.async wrote through the generic proxy; the MMA reads via async
-    if (cin_tma) {
+    cp_async_wait_all();  // the per-row C_in copies, when C is not TMA-addressable
+    {
       const long long t0 = clock64();
-      while (!mbar_try_wait(smem_addr(cin_bar), cin_phase)) {
+      while (!mbar_try_wait(smem_addr(ld_bar), ld_phase)) {
         if (clock64() - t0 > kWaitBudgetCycles) {
           record_error(TB_ERR_DEVICE_TIMEOUT, kSiteEpilogue);
           break;
         }
       }
-      cin_phase ^= 1u;
+      ld_phase ^= 1u;
     }
+    fence_proxy_async_smem();  // cp.async wrote through the generic proxy; the MMA reads via async
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -1441,8 +1432,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 std::atomic<bool> g_small_attr_set[2][2][kMaxDevices];
 
 template <int BN, typename OutT>
-tbStatus launch_small_bn(const tb_matmul_plan* plan, const KParams& kp, const CUtensorMap& tcm,
-                         const void* A, int64_t lda,
+tbStatus launch_small_bn(const tb_matmul_plan* plan, const KParams& kp, const CUtensorMap& ta,
+                         const CUtensorMap& tb_, const CUtensorMap& tcm, const void* A, int64_t lda,
                          const void* B, int64_t ldb, cudaStream_t stream, int ot) {
   auto kern = tb_gemm_small_kernel<BN, OutT>;
   constexpr size_t smem = SmallCfg<BN, OutT>::kSmem;
@@ -1468,8 +1459,8 @@ tbStatus launch_small_bn(const tb_matmul_plan* plan, const KParams& kp, const CU
     tab.kvalid[pos] = (int16_t)(e.nkb > 0 ? e.k_end - e.k_begin : 0);
     tab.part[pos] = (int16_t)e.part;
   }
-  kern<<<(unsigned)plan->grid, 128, smem, stream>>>(kp, tab, tcm, static_cast<const uint16_t*>(A), lda,
-                                                    static_cast<const uint16_t*>(B), ldb);
+  (void)A; (void)lda; (void)B; (void)ldb;
+  kern<<<(unsigned)plan->grid, 128, smem, stream>>>(kp, tab, ta, tb_, tcm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     return tb_fail(TB_ERR_CUDA, std::string("tb_gemm_small launch: ") + cudaGetErrorString(e));
@@ -1477,10 +1468,11 @@ tbStatus launch_small_bn(const tb_matmul_plan* plan, const KParams& kp, const CU
 }
 
 template <typename OutT>
-tbStatus launch_small(const tb_matmul_plan* plan, const KParams& kp, const CUtensorMap& tcm, const void* A,
-                      int64_t lda, const void* B, int64_t ldb, cudaStream_t stream, int ot) {
-  return plan->cta_n == 64 ? launch_small_bn<64, OutT>(plan, kp, tcm, A, lda, B, ldb, stream, ot)
-                           : launch_small_bn<128, OutT>(plan, kp, tcm, A, lda, B, ldb, stream, ot);
+tbStatus launch_small(const tb_matmul_plan* plan, const KParams& kp, const CUtensorMap& ta,
+                      const CUtensorMap& tb_, const CUtensorMap& tcm, const void* A, int64_t lda,
+                      const void* B, int64_t ldb, cudaStream_t stream, int ot) {
+  return plan->cta_n == 64 ? launch_small_bn<64, OutT>(plan, kp, ta, tb_, tcm, A, lda, B, ldb, stream, ot)
+                           : launch_small_bn<128, OutT>(plan, kp, ta, tb_, tcm, A, lda, B, ldb, stream, ot);
 }
 
 tbStatus pack_rows_f16(const void* src, int64_t ld_src, void* dst, int64_t ld_dst, int64_t rows,
@@ -1607,15 +1599,16 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   CUtensorMap ta, tbm;
   memset(&ta, 0, sizeof(ta));
   memset(&tbm, 0, sizeof(tbm));
-  if (plan->small) {
-    // the latency kernel stages operands with cp.async: no tensor maps
-  } else if (d.a_col_major)  // storage k × m (m contiguous): [64 k × 64 m] boxes
+  if (plan->small)  // the latency kernel: [128 m × 64 k] A boxes (row-major only)
+    st = encode_f16_2d(&ta, A, d.m, d.k, lda, kCtaM, "A");
+  else if (d.a_col_major)  // storage k × m (m contiguous): [64 k × 64 m] boxes
     st = encode_f16_2d(&ta, A, d.k, d.m, lda, (uint32_t)plan->kb, "A");
   else                // storage m × k: [128 m × 64 k] boxes
     st = encode_f16_2d(&ta, A, d.m, d.k, lda, kCtaM, "A");
   if (st != TB_OK) return st;
-  if (plan->small) {
-  } else if (d.b_col_major)  // storage n × k (k contiguous): [BN/G n × 64 k] boxes; the 256 × 512
+  if (plan->small)  // [kSmallK k × 64 n] B boxes
+    st = encode_f16_2d(&tbm, B, d.k, d.n, ldb, (uint32_t)kSmallK, "B");
+  else if (d.b_col_major)  // storage n × k (k contiguous): [BN/G n × 64 k] boxes; the 256 × 512
                       // pair tile loads its 256 columns per CTA as two 128-row boxes
     st = encode_f16_2d(&tbm, B, d.n, d.k, ldb,
                        (uint32_t)(plan->cta_n > 256 ? 128 : plan->cta_n / plan->ctas_per_tile), "B");
@@ -1728,8 +1721,8 @@ tbStatus tb_launch_ex(const tb_matmul_plan* plan, const void* A, int64_t lda, co
   }
 
   if (plan->small)
-    st = d.c_dtype == TB_F16 ? launch_small<__half>(plan, kp, tcm, A, lda, B, ldb, stream, 1)
-                             : launch_small<float>(plan, kp, tcm, A, lda, B, ldb, stream, 0);
+    st = d.c_dtype == TB_F16 ? launch_small<__half>(plan, kp, ta, tbm, tcm, A, lda, B, ldb, stream, 1)
+                             : launch_small<float>(plan, kp, ta, tbm, tcm, A, lda, B, ldb, stream, 0);
   else
     st = d.c_dtype == TB_F16 ? dispatch_tile<__half>(plan, ta, tbm, tcm, kp, stream, 1)
                              : dispatch_tile<float>(plan, ta, tbm, tcm, kp, stream, 0);
