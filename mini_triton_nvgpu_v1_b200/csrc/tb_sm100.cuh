@@ -100,13 +100,20 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32
 }
 
 // 2-D tiled store of one shared-memory box to global memory (bulk group).
-// Elements outside the tensor are not written.
+// Elements outside the tensor are not written. The output is written once
+// and not read again by the kernel: the stored lines are marked first to
+// leave L2 (evict_first), so they do not push out the A/B panel slices
+// other CTAs are about to read (measured +1–3 % over 300 back-to-back
+// 8192³ launches, no change over 20).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x,
                                              int32_t y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(src), "r"(x), "r"(y)
-               : "memory");
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(x), "r"(y), "l"(policy)
+      : "memory");
 }
 // Element-wise f32 add of one shared-memory box into global memory (TMA
 // reduction; performed at L2, no read-modify-write round trip).
