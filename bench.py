@@ -56,7 +56,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kshard", action="store_true",
                     help="gemm8192 at N>1: skip the extra K-sharded split-K measurement")
-    ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "splitk", "sweep"],
+    ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "splitk", "sweep", "cublas"],
                     help="gemm8192: the headline 8192^3 N-sharded GEMM; splitk: the skinny "
                          "512x512x65536 split-K config (K-sharded + reduce-scatter at N>1)")
     ap.add_argument("--only", default=None, help="sweep: only the configs whose name contains this")
@@ -757,6 +757,41 @@ def run_sweep(args):
     return 0
 
 
+def run_cublas(args):
+    """Context only, not the product: cuBLAS (through torch) on the same
+    8192³ inputs — f16·f16 → f32 with beta = 0 (torch.mm, out_dtype f32) and
+    with C += A·B (aten.addmm.dtype, f32 C) — against this library's run, all
+    in one process, over 20 and 300 back-to-back calls."""
+    import torch
+    import mini_triton_nvgpu_v1_b200 as tb
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(4)
+    A = (torch.randn(M, K, device=dev, generator=g) * 0.1).half()
+    B = (torch.randn(K, N_PER_GPU, device=dev, generator=g) * 0.1).half()
+    C = torch.zeros(M, N_PER_GPU, device=dev)
+    fns = {
+        "tb.matmul C += A·B (this library)": lambda: tb.matmul(A, B, C, **BLOCK),
+        "cuBLAS torch.mm f16->f32 (beta = 0)": lambda: torch.mm(A, B, out_dtype=torch.float32),
+        "cuBLAS aten.addmm.dtype f16->f32, C += A·B": lambda: torch.ops.aten.addmm.dtype(C, A, B, torch.float32),
+    }
+    for name, f in fns.items():
+        for _ in range(10):
+            f()
+        torch.cuda.synchronize()
+        res = {}
+        for n in (20, 300):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(n):
+                f()
+            e1.record()
+            torch.cuda.synchronize()
+            res[f"tflops_{n}_calls"] = round(2.0 * M * N_PER_GPU * K / (e0.elapsed_time(e1) / n * 1e-3) / 1e12, 1)
+        print(json.dumps({"workload": "cublas_context", "impl": name, **res}), flush=True)
+        time.sleep(2)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -765,6 +800,8 @@ def main():
         return run_splitk(args)
     if args.workload == "sweep":
         return run_sweep(args)
+    if args.workload == "cublas":
+        return run_cublas(args)
     return run_ours(args)
 
 
