@@ -789,6 +789,36 @@ def run_cublas(args):
             res[f"tflops_{n}_calls"] = round(2.0 * M * N_PER_GPU * K / (e0.elapsed_time(e1) / n * 1e-3) / 1e12, 1)
         print(json.dumps({"workload": "cublas_context", "impl": name, **res}), flush=True)
         time.sleep(2)
+    # the skinny split-K config: time per call with L2 flushed before each
+    g.manual_seed(6)
+    A = (torch.rand(SK_M, SK_K, device=dev, generator=g) * 2 - 1).half()
+    B = (torch.rand(SK_K, SK_N, device=dev, generator=g) * 2 - 1).half()
+    C = torch.zeros(SK_M, SK_N, device=dev)
+    ws = torch.empty(16 << 20, dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    fns = {
+        "tb.matmul split_k=16 parallel (this library)": lambda: tb.matmul(
+            A, B, C, split_k=SK_SPLIT, reduction_mode="split_k_parallel", **SK_BLOCK),
+        "tb.matmul split_k=16 serial (this library)": lambda: tb.matmul(
+            A, B, C, workspace=ws, split_k=SK_SPLIT, reduction_mode="split_k_serial", **SK_BLOCK),
+        "cuBLAS aten.addmm.dtype f16->f32, C += A·B": lambda: torch.ops.aten.addmm.dtype(C, A, B, torch.float32),
+        "cuBLAS torch.mm f16->f32 (beta = 0)": lambda: torch.mm(A, B, out_dtype=torch.float32),
+    }
+    for name, f in fns.items():
+        for _ in range(5):
+            f()
+        ts = []
+        for _ in range(30):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            f()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        ts.sort()
+        print(json.dumps({"workload": "cublas_context_splitk", "impl": name, "us_median": round(ts[15], 1),
+                          "us_min": round(ts[0], 1)}), flush=True)
     return 0
 
 
