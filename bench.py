@@ -789,6 +789,27 @@ def run_cublas(args):
             res[f"tflops_{n}_calls"] = round(2.0 * M * N_PER_GPU * K / (e0.elapsed_time(e1) / n * 1e-3) / 1e12, 1)
         print(json.dumps({"workload": "cublas_context", "impl": name, **res}), flush=True)
         time.sleep(2)
+    # f16-output configs of the sweep (C += A·B with f16 C), back-to-back calls
+    for (mm, nn, kk, kn) in ((2048, 2048, 2048, dict(block_m=256, block_n=256, block_k=64, persistent=True,
+                                                    num_ctas=148)),
+                             (4096, 4096, 4096, dict(block_m=128, block_n=128, block_k=64))):
+        g.manual_seed(2)
+        A = (torch.rand(mm, kk, device=dev, generator=g) * 2 - 1).half()
+        B = (torch.rand(kk, nn, device=dev, generator=g) * 2 - 1).half()
+        C = torch.zeros(mm, nn, device=dev, dtype=torch.float16)
+        for name, f in ((f"tb.matmul {mm}^3 f16 C (this library)", lambda: tb.matmul(A, B, C, **kn)),
+                        (f"cuBLAS torch.addmm {mm}^3 f16 C", lambda: torch.addmm(C, A, B))):
+            for _ in range(10):
+                f()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(100):
+                f()
+            e1.record()
+            torch.cuda.synchronize()
+            print(json.dumps({"workload": "cublas_context_f16", "impl": name,
+                              "us_per_call": round(e0.elapsed_time(e1) / 100 * 1e3, 2)}), flush=True)
     # the skinny split-K config: time per call with L2 flushed before each
     g.manual_seed(6)
     A = (torch.rand(SK_M, SK_K, device=dev, generator=g) * 2 - 1).half()
