@@ -93,10 +93,11 @@ typedef struct tb_matmul_desc {
    * b_col_major: B is k × n column-major, ldb >= k (B^T row-major). */
   int32_t a_col_major, b_col_major;
   /* 1: bitwise-repeatable runs. By default (0) a plain f32-output plan whose
-   * work items leave the last wave of SMs partly idle cuts its last items
-   * into K pieces that other SMs compute and reduce-add into C (results
-   * within the f32 tolerance, summation order not fixed). No counterpart in
-   * the reference. */
+   * work items leave the last wave of SMs partly idle (after at least one
+   * whole wave) spreads the K work of its last items evenly over the SMs
+   * (a stream-K tail: partial tiles reduce-added into C; results within the
+   * f32 tolerance, summation order not fixed). No counterpart in the
+   * reference. */
   int32_t deterministic;
 } tb_matmul_desc;
 

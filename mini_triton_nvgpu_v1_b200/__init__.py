@@ -103,7 +103,7 @@ class KernelConfig:
     # operand storage: column-major A (m × k, lda >= m) / B (k × n, ldb >= k)
     a_col_major: bool = False
     b_col_major: bool = False
-    # bitwise-repeatable runs: no K pieces reduce-added into C for tail balancing
+    # bitwise-repeatable runs: no stream-K tail (partial tiles reduce-added into C)
     deterministic: bool = False
 
     def to_desc(self) -> _capi.tb_matmul_desc:
@@ -334,7 +334,7 @@ def matmul(A, B, Cm, *, block_m: int = 128, block_n: int = 256, block_k: int = 6
     and ``clamp`` ((lo, hi)) are fused epilogue expressions applied, in that
     order, to the complete sum before the output conversion.
     ``deterministic=True`` keeps every tile's sum in one fixed order (no
-    tail-balancing K pieces), so repeated runs are bitwise equal."""
+    stream-K tail), so repeated runs are bitwise equal."""
     import torch
     # Fast path: everything that decides the plan and the leading dimensions
     # is in the key, so a hit skips validation and plan construction.
